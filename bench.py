@@ -1,0 +1,505 @@
+"""Benchmark of the prioritized-replay hot path on B200.
+
+Default workload (N=1): the high-UTD replay loop on 1,000,000 x 74 float32
+transitions (fields obs32/action8/reward1/next_obs32/done1, rows ~N(0,1),
+done in {0,1}), priorities (|N(0,1)|+1e-6)^0.6: one step = add 1 transition +
+32 x (sample batch 256 with beta 0.4 -> update 256 TD errors |N(0,1)|).
+Metric: sampled transitions per second (sample + gather + IS weights).
+
+  value     device-resident: the step captured in a CUDA graph, CUDA events
+            around exactly K replays after W warm-up replays (max over ranks).
+  e2e       the same loop through the public PERBuffer API, eager, with the
+            step's inputs copied from pinned host memory and the sampled
+            batches (rows, idx, w) copied back to pinned host memory.
+  roofline  the fused sample kernel alone on the same store: algorithmic
+            bytes (8*row_dim + 16 per draw) over its CUDA-event launch time,
+            against the measured HBM copy peak.
+  sweep     the same kernel over batch 32..65,536 on heavy-tailed
+            priorities (lognormal(0,2), 1% exact zeros).
+  cpu_baseline  the oracle (CPU restatement of the reference's torch
+            backend, C, all host threads) on a bounded sample of the same loop.
+
+--impl reference times that CPU implementation alone on the same loop.
+N>1 (torchrun): every rank runs an independent replica of the loop on its own
+GPU (no collective on the data path); value = all ranks' transitions / max time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "triton-per_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+FIELDS_74 = {"obs": 32, "action": 8, "reward": 1, "next_obs": 32, "done": 1}
+CAPACITY = 1_000_000
+ROW_DIM = 74
+BATCH = 256
+ROUNDS = 32
+BETA = 0.4
+SWEEP = [32, 128, 512, 2048, 8192, 32768, 65536]
+METRIC = "sampled transitions/s (sample+gather+IS)"
+UNIT = "transitions/s"
+
+
+def algo_bytes(batch: int, row_dim: int) -> int:
+    """Algorithmic bytes of one fused sample: row read + row write + idx + w + uniform."""
+    return batch * (8 * row_dim + 16)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during timing."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            if self.t:
+                self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- distributed
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- workload
+def make_store(device, seed, priorities="absnormal"):
+    from per_b200 import PERBuffer
+
+    buf = PERBuffer(CAPACITY, FIELDS_74, device=device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    chunk = 250_000
+    for s in range(0, CAPACITY, chunk):
+        n = min(chunk, CAPACITY - s)
+        batch = {k: torch.randn(n, d, generator=g, device=device)
+                 for k, d in FIELDS_74.items() if k != "done"}
+        batch["done"] = (torch.rand(n, 1, generator=g, device=device) < 0.5).float()
+        buf.add(batch)
+    if priorities == "absnormal":
+        leaves = (torch.randn(CAPACITY, generator=g, device=device).abs() + 1e-6) ** 0.6
+    else:  # heavy-tailed with 1% exact zeros
+        leaves = torch.empty(CAPACITY, device=device).log_normal_(0.0, 2.0, generator=g)
+        zeros = torch.randperm(CAPACITY, generator=g, device=device)[: CAPACITY // 100]
+        leaves[zeros] = 0.0
+    buf.priorities[:CAPACITY] = leaves
+    buf.rebuild_sums()
+    torch.cuda.synchronize()
+    return buf
+
+
+def utd_step(buf, row, td):
+    """One step of the high-UTD loop: add 1, then 32 x (sample 256 -> update 256)."""
+    buf.add(row)
+    for r in range(ROUNDS):
+        _, idx, _ = buf.sample(BATCH, BETA)
+        buf.update_priorities(idx, td[r])
+
+
+def capture(fn, warm=3):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_replays(g, iters, world):
+    st = torch.cuda.current_stream()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    a.record(st)
+    for _ in range(iters):
+        g.replay()
+    b.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    return a.elapsed_time(b)  # ms
+
+
+def kernel_time_us(buf, batch, reps=20, launches=16, seed=7):
+    """Average CUDA-event time of one fused-sample launch (graph of `launches`)."""
+    g0 = torch.Generator(device=buf.device).manual_seed(seed)
+    rands = [torch.rand(batch, generator=g0, device=buf.device) for _ in range(launches)]
+
+    def fn():
+        for r in rands:
+            buf.sample_from_uniforms(r, BETA)
+
+    g = capture(fn, warm=2)
+    for _ in range(3):
+        g.replay()
+    ms = time_replays(g, reps, 1)
+    return ms * 1000.0 / (reps * launches)
+
+
+def update_time_us(buf, n, reps=20, launches=16, seed=8):
+    g0 = torch.Generator(device=buf.device).manual_seed(seed)
+    idxs = [torch.randint(0, CAPACITY, (n,), generator=g0, device=buf.device) for _ in range(launches)]
+    tds = [torch.randn(n, generator=g0, device=buf.device).abs() for _ in range(launches)]
+
+    def fn():
+        for i, t in zip(idxs, tds):
+            buf.update_priorities(i, t)
+
+    g = capture(fn, warm=2)
+    for _ in range(3):
+        g.replay()
+    ms = time_replays(g, reps, 1)
+    return ms * 1000.0 / (reps * launches)
+
+
+def e2e_loop(buf, steps, warmup, world, seed=9):
+    """Public API, eager, host buffers: H2D of the step's inputs from pinned
+    memory, D2H of every sampled batch (rows, idx, w) into pinned memory."""
+    dev = buf.device
+    g = np.random.default_rng(seed)
+    h_row = {k: torch.from_numpy(g.standard_normal((1, d), dtype=np.float32)).pin_memory()
+             for k, d in FIELDS_74.items()}
+    h_td = torch.from_numpy(np.abs(g.standard_normal((ROUNDS, BATCH))).astype(np.float32)).pin_memory()
+    h_rows = torch.empty(ROUNDS, BATCH, ROW_DIM).pin_memory()
+    h_idx = torch.empty(ROUNDS, BATCH, dtype=torch.int64).pin_memory()
+    h_w = torch.empty(ROUNDS, BATCH).pin_memory()
+    h2d = sum(v.numel() * 4 for v in h_row.values()) + h_td.numel() * 4
+    d2h = h_rows.numel() * 4 + h_idx.numel() * 8 + h_w.numel() * 4
+
+    def step():
+        row = {k: v.to(dev, non_blocking=True) for k, v in h_row.items()}
+        td = h_td.to(dev, non_blocking=True)
+        buf.add(row)
+        for r in range(ROUNDS):
+            views, idx, w = buf.sample(BATCH, BETA)
+            buf.update_priorities(idx, td[r])
+            h_rows[r].copy_(torch.cat([views[k] for k in FIELDS_74], dim=1), non_blocking=True)
+            h_idx[r].copy_(idx, non_blocking=True)
+            h_w[r].copy_(w, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    st = torch.cuda.current_stream()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    a.record(st)
+    for _ in range(steps):
+        step()
+    b.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b), world)
+    return ms / steps, h2d, d2h
+
+
+# ---------------------------------------------------------------- CPU side
+def cpu_loop(seconds=None, steps=None, warmup=0, threads=None):
+    """The oracle (reference torch-backend algorithm, C) on the same loop.
+
+    Returns (transitions/s, steps timed, threads)."""
+    from oracle import oracle
+
+    threads = threads or os.cpu_count() or 1
+    rng = np.random.default_rng(3)
+    cap = CAPACITY
+    nb = -(-cap // 1024)
+    leaves = np.zeros(nb * 1024, np.float32)
+    leaves[:cap] = np.power(np.abs(rng.standard_normal(cap)).astype(np.float32) + np.float32(1e-6),
+                            np.float32(0.6))
+    storage = rng.standard_normal((cap, ROW_DIM), dtype=np.float32)
+    bsums = oracle.block_sums(leaves)
+    st = oracle.OracleStore.__new__(oracle.OracleStore)
+    st.capacity, st.alpha, st.eps, st.row_dim = cap, 0.6, 1e-6, ROW_DIM
+    st.num_blocks, st.capacity_padded = nb, nb * 1024
+    st.priorities, st.block_sums, st.storage = leaves, bsums, storage
+    st.max_priority, st.size, st.cursor = np.float32(1.0), cap, 0
+    st._offsets = {"row": (0, ROW_DIM)}
+    st.fields = {"row": ROW_DIM}
+    row = rng.standard_normal((1, ROW_DIM), dtype=np.float32)
+    td = np.abs(rng.standard_normal((ROUNDS, BATCH))).astype(np.float32)
+    csum = np.empty(cap, np.float32)
+
+    def one_step():
+        st.add({"row": row})
+        for r in range(ROUNDS):
+            rand = rng.random(BATCH, dtype=np.float32)
+            oracle.lib().oracle_cumsum(st.priorities, cap, csum, threads)
+            idx, w, _ = oracle.sample_from_csum(st.priorities, csum, cap, st.size, rand, BETA, threads)
+            _ = st.storage[idx]  # gather
+            st.update_priorities(idx, td[r])
+
+    for _ in range(warmup):
+        one_step()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        one_step()
+        n += 1
+        el = time.perf_counter() - t0
+        if steps is not None and n >= steps:
+            break
+        if seconds is not None and el >= seconds:
+            break
+    return ROUNDS * BATCH * n / el, n, threads
+
+
+# ---------------------------------------------------------------- main
+def traffic_from_profiles():
+    """dram bytes per launch of the fused sample at batch 256, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "sample_kernel_1Mx74.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch_b256:"):
+                return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    v, n, threads = cpu_loop(steps=max(1, args.steps), warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ROUNDS * BATCH / v * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "utd-1Mx74: add 1 + 32 x (sample 256 beta 0.4 -> update 256)",
+                   "capacity": CAPACITY, "row_dim": ROW_DIM, "batch": BATCH, "rounds": ROUNDS,
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{n} full steps ({n * ROUNDS} sample+update rounds) of the loop, "
+                                   "oracle restatement of the reference torch backend in C"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    buf = make_store(dev, seed=1 + rank)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    td = torch.randn(ROUNDS, BATCH, generator=g, device=dev).abs()
+    row = {k: torch.randn(1, d, generator=g, device=dev) for k, d in FIELDS_74.items()}
+
+    graph = capture(lambda: utd_step(buf, row, td))
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms = time_replays(graph, args.steps, world)
+    ms = max_over_ranks(ms, world)
+    ms_per_step = ms / args.steps
+    total = ROUNDS * BATCH * world
+    value = total / (ms_per_step / 1e3)
+    st = buf.status()
+    if st["errors"] or st["timeouts"]:
+        raise SystemExit(f"device status reports errors: {st}")
+
+    # kernel-level: fused sample at the loop's batch, update at the loop's size
+    peak, peak_kind = peaks()
+    k_us = kernel_time_us(buf, BATCH)
+    u_us = update_time_us(buf, BATCH)
+    ab = algo_bytes(BATCH, ROW_DIM)
+    achieved = ab / (k_us * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": traffic_from_profiles(),
+                "peak_source": peak_kind, "kernel": "per_sample_kernel",
+                "kernel_us": k_us, "algo_bytes_per_launch": ab}
+
+    sweep = None
+    if not args.no_sweep and rank == 0:
+        graph = None
+        heavy = make_store(dev, seed=5, priorities="heavy")
+        sweep = []
+        for b in SWEEP:
+            us = kernel_time_us(heavy, b, reps=10, launches=8)
+            gbs = algo_bytes(b, ROW_DIM) / (us * 1e-6) / 1e9
+            sweep.append({"batch": b, "us": round(us, 3), "gbs": round(gbs, 1),
+                          "frac": round(gbs / peak, 4),
+                          "samples_per_s": round(b / (us * 1e-6))})
+        storm = update_time_us(heavy, 65536, reps=5, launches=4)
+        sweep.append({"update_storm_65536_us": round(storm, 2)})
+        del heavy
+        torch.cuda.empty_cache()
+
+    e2e = None
+    if not args.no_e2e:
+        e_ms, h2d, d2h = e2e_loop(buf, steps=max(5, min(args.steps, 50)), warmup=3, world=world)
+        e2e = {"value": ROUNDS * BATCH * world / (e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, n, threads = cpu_loop(seconds=args.cpu_seconds, warmup=1)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{n} steps ({n * ROUNDS} sample 256 + update 256 rounds) of the same "
+                         "loop, oracle (reference torch-backend algorithm) in C"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "utd-1Mx74: add 1 + 32 x (sample 256 beta 0.4 -> update 256)",
+                       "capacity": CAPACITY, "row_dim": ROW_DIM, "batch": BATCH,
+                       "rounds": ROUNDS, "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "storage 296 MB > 126 MB L2 (tree 4 MB stays resident)",
+                       "timing": "CUDA graph of one step, CUDA events, max over ranks"},
+            "update_us": u_us,
+            "roofline": roofline,
+            "sweep": sweep,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "gpu_launches": (1 + 2 * ROUNDS) * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        graph = None
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,172 @@
+/*
+ * per_b200.h - C ABI of the B200 prioritized-replay engine.
+ *
+ * The engine keeps the two-level priority store of triton-per
+ * (src/triton_per/buffer.py:20-63: float32 leaf priorities padded to
+ * BLOCK_P = 1024 per block, plus one float32 partial sum per block) and widens
+ * it into a 32-ary sum tree whose fan-out equals the warp width:
+ *
+ *   level 0   leaf priorities                       float32[capacity_padded]
+ *   level 1   sums of 32 leaves ("chunks")          float32
+ *   level 2   sums of 32 chunks = 1024-leaf blocks  float32   (== block_sums)
+ *   level k   sums of 32 level k-1 nodes            float32   (only when needed)
+ *
+ * Each level step of a sample is one coalesced 128-byte warp load plus a warp
+ * scan; the highest level the sampler needs ("top level", at most
+ * PER_TOP_MAX nodes) is staged as a float64 prefix in shared memory.
+ *
+ * Conventions of every entry point:
+ *   - plain device pointers and sizes; no framework types;
+ *   - the caller allocates every buffer (per_layout() gives the sizes) and
+ *     keeps ownership; the library never allocates or frees device memory in
+ *     these entry points and never synchronises the host;
+ *   - all work is enqueued on `stream` (a cudaStream_t passed as void*,
+ *     NULL = legacy default stream), in stream order, like the reference's
+ *     kernels on the caller's current stream;
+ *   - return 0 (PER_OK) or a PER_ERR_* code; per_error_string() names it and
+ *     per_last_cuda_error() gives the CUDA error code behind PER_ERR_CUDA;
+ *   - calls on one store must not overlap on the GPU (one stream, or events);
+ *     the reference buffer is single-threaded in the same way.
+ *
+ * Device-side events that the host cannot see at launch time (barrier
+ * timeouts, indices out of range, rounding fallbacks) are counted in the
+ * store's `status` words; see PER_STATUS_*.
+ */
+#ifndef PER_B200_H
+#define PER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PER_ABI_VERSION 1
+
+#define PER_BLOCK_P 1024   /* leaves per block: reference buffer.py:20 BLOCK_P */
+#define PER_FANOUT 32      /* children per tree node (= warp width) */
+#define PER_LOG_FANOUT 5
+#define PER_MAX_LEVELS 7   /* levels 0..6: up to 2^30 leaves */
+#define PER_TOP_MAX 4096   /* max nodes of the level staged in shared memory */
+#define PER_MAX_FIELDS 16  /* max fields of one add() call */
+#define PER_STATUS_WORDS 16
+#define PER_MAX_GRID 4096  /* max CTAs of one grid-synchronised launch */
+#define PER_SCRATCH_BYTES (256 + 4 * PER_MAX_GRID)
+
+/* return codes */
+#define PER_OK 0
+#define PER_ERR_INVALID_ARGUMENT 1
+#define PER_ERR_NULL_POINTER 2
+#define PER_ERR_EMPTY 3
+#define PER_ERR_TOO_LARGE 4
+#define PER_ERR_MISALIGNED 5
+#define PER_ERR_CUDA 6
+#define PER_ERR_NO_DEVICE 7
+
+/* status[] word indices (device uint32 counters / bit sets) */
+#define PER_STATUS_ERRORS 0        /* bit set of PER_EVT_* error bits */
+#define PER_STATUS_FALLBACKS 1     /* draws that met a rounding / overflow fallback in the tree walk */
+#define PER_STATUS_ZERO_WALKS 2    /* draws whose clamped slot had p == 0 and walked back */
+#define PER_STATUS_CLAMPS 3        /* draws clamped to size-1 */
+#define PER_STATUS_BAD_INDICES 4   /* update indices outside [0, capacity) (skipped) */
+#define PER_STATUS_TIMEOUTS 5      /* grid-barrier waits that gave up */
+#define PER_STATUS_FOREIGN 6       /* sharded: indices owned by another shard (skipped) */
+
+#define PER_EVT_BARRIER_TIMEOUT 0x1u
+#define PER_EVT_EMPTY_BUFFER 0x2u
+#define PER_EVT_BAD_INDEX 0x4u
+#define PER_EVT_INCONSISTENT_TREE 0x8u
+#define PER_EVT_PEER_TIMEOUT 0x10u
+
+/* Sizes of every array of a store of `capacity` slots. */
+typedef struct per_layout {
+  int64_t capacity;
+  int64_t capacity_padded;              /* ceil(capacity / 1024) * 1024 */
+  int64_t num_blocks;                   /* ceil(capacity / 1024) */
+  int32_t num_levels;                   /* levels maintained, >= 3 */
+  int32_t top_level;                    /* level staged in shared memory by the sampler */
+  int64_t level_nodes[PER_MAX_LEVELS];  /* live nodes per level: ceil(capacity / 32^k) */
+  int64_t level_len[PER_MAX_LEVELS];    /* allocated float32 entries per level (padded) */
+  int64_t scratch_bytes;                /* bytes of `scratch` */
+} per_layout_t;
+
+/* One replay store: device pointers owned by the caller. */
+typedef struct per_store {
+  float* levels[PER_MAX_LEVELS];    /* levels[0] = priorities, levels[2] = block sums */
+  uint32_t* claims[PER_MAX_LEVELS]; /* zeroed scratch, level_len[k] words each, for k < num_levels */
+  int64_t level_len[PER_MAX_LEVELS];
+  int32_t num_levels;
+  int32_t top_level;
+  int64_t capacity;
+  float* storage;          /* float32 rows, row i at storage + i * row_stride */
+  int64_t row_dim;
+  int64_t row_stride;      /* elements, >= row_dim */
+  int64_t* size_cursor;    /* device int64[2]: live size, ring cursor */
+  float* max_priority;     /* device float32 scalar, already ^alpha (buffer.py:59) */
+  uint32_t* status;        /* device uint32[PER_STATUS_WORDS] */
+  void* scratch;           /* device, scratch_bytes, zeroed once at creation */
+  int64_t scratch_bytes;
+  float alpha;             /* buffer.py:29 */
+  float eps;               /* buffer.py:30 */
+} per_store_t;
+
+/* One field of an add() batch: rows [n, dim] of float32 with a row stride. */
+typedef struct per_field {
+  const float* data;
+  int64_t dim;
+  int64_t stride;      /* elements between consecutive rows of `data` */
+  int64_t col_offset;  /* first column of this field inside a storage row */
+} per_field_t;
+
+/* Fill `out` with the array sizes for a store of `capacity` slots.
+ * Replaces the sizing in reference buffer.py:48-54. */
+int per_layout(int64_t capacity, per_layout_t* out);
+
+/* Fused prioritized sample: tree search + row gather + importance weights
+ * normalised by the batch maximum, in one launch.
+ * For j < batch: u_j = rand[j] * total (float32), idx[j] = first slot whose
+ * inclusive priority prefix exceeds u_j, clamped to size-1; out row j =
+ * storage row idx[j]; w[j] = (size * p / total)^-beta / max_j(...).
+ * Replaces reference buffer.py:82-94 (sample, w / w.max()), buffer.py:107-130
+ * (_sample_triton) and kernels/fused.py:16-52 (fused_sample_kernel) with
+ * kernels/sampling.py:16-56 (_find_index).
+ * `out_stride` is in elements (>= row_dim). */
+int per_sample_fused(const per_store_t* store, const float* rand, int64_t batch,
+                     float beta, float* out, int64_t out_stride, int64_t* idx,
+                     float* w, void* stream);
+
+/* p_i <- (|td_i| + eps)^alpha for every i, max-priority tracking, and exact
+ * recomputation of every touched chunk / block / upper node. Duplicate
+ * indices resolve deterministically: the last occurrence wins.
+ * Replaces reference buffer.py:133-162 (update_priorities, including the
+ * periodic exact refresh) and kernels/update.py:14-35 (update_kernel). */
+int per_update_priorities(const per_store_t* store, const int64_t* idx,
+                          const float* td, int64_t n, void* stream);
+
+/* Ring insert of n transitions at the device cursor: rows are written from
+ * the field arrays, new leaves get the current max priority, touched tree
+ * nodes are recomputed exactly, and size/cursor advance on the device.
+ * Replaces reference buffer.py:66-79 (add) without its host synchronisation. */
+int per_add(const per_store_t* store, const per_field_t* fields,
+            int32_t n_fields, int64_t n, void* stream);
+
+/* Recompute every tree level above the leaves from the leaves and clear the
+ * claim scratch. Call after writing priorities directly.
+ * Replaces the exact refresh of reference buffer.py:156-162. */
+int per_rebuild_sums(const per_store_t* store, void* stream);
+
+/* Human-readable name of a PER_* return code. */
+const char* per_error_string(int code);
+
+/* cudaError_t value behind the last PER_ERR_CUDA returned on this thread. */
+int per_last_cuda_error(void);
+
+/* PER_ABI_VERSION of the loaded library. */
+int per_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PER_B200_H */

@@ -1,0 +1,283 @@
+"""CUDA engine vs the oracle and the reference's golden vectors (B200).
+
+Indices: bit-exact except float32 prefix-boundary ties (|u - prefix| <= 1 ulp,
+counted). Rows: bit-exact. IS weights: within 1e-6 relative. Tree sums: within
+1e-5 relative of the exact sums of the leaves.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from helpers import SUM_RTOL, check_sample, check_tree, make_buffer, packed_rows
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def ulps(a, b):
+    a = np.asarray(a, np.float32).view(np.int32).astype(np.int64)
+    b = np.asarray(b, np.float32).view(np.int32).astype(np.int64)
+    return np.abs(a - b)
+
+
+@pytest.mark.parametrize("name", sorted(cases.SAMPLE_CASES))
+def test_sample_matches_golden(name):
+    c = cases.SAMPLE_CASES[name]()
+    g = np.load(os.path.join(GOLDEN, f"sample_{name}.npz"))
+    buf = make_buffer(c["capacity"], c["fields"], c["rows"], c["leaves"])
+    assert buf.size == c["size"]
+    check_tree(buf)
+    rows = packed_rows(c["rows"], c["fields"])
+    r = check_sample(buf, rows, c["leaves"], c["size"], c["rand"], c["beta"],
+                     golden_idx=g["idx"], tag=name)
+    print(f"PARITY {name}: {r}")
+    if name != "ties":
+        assert r["excused"] <= max(2, r["n"] // 100)
+    assert buf.status()["errors"] == 0
+
+
+def test_config1_round_trip_matches_golden():
+    """CPU config of the reference: sample 256 -> update 256 (10% dups) -> sample 256."""
+    c = cases.case_config1()
+    g = np.load(os.path.join(GOLDEN, "sample_config1.npz"))
+    buf = make_buffer(c["capacity"], c["fields"], c["rows"], c["leaves"])
+    rows = packed_rows(c["rows"], c["fields"])
+    check_sample(buf, rows, c["leaves"], c["size"], c["rand"], c["beta"], golden_idx=g["idx"])
+    upd = torch.from_numpy(g["upd_idx"]).cuda()
+    buf.update_priorities(upd, torch.from_numpy(c["td"]).cuda())
+    leaves = buf.priorities.cpu().numpy()
+    np.testing.assert_allclose(leaves[g["upd_uniq"]], g["upd_leaves"], rtol=1e-6)
+    np.testing.assert_allclose(buf.block_sums.cpu().numpy(), g["upd_block_sums"], rtol=SUM_RTOL)
+    assert ulps(buf._max_priority.item(), g["upd_max_priority"]).max() <= 2
+    check_tree(buf)
+    lv = leaves[: c["capacity"]]
+    check_sample(buf, rows, lv, c["size"], c["rand2"], c["beta"])
+
+
+@pytest.mark.parametrize("name,fn", [("update_dups", cases.case_update_dups),
+                                     ("update_storm", cases.case_update_storm)])
+def test_update_matches_golden(name, fn):
+    c = fn()
+    g = np.load(os.path.join(GOLDEN, name + ".npz"))
+    buf = make_buffer(c["capacity"], {"x": 1}, None, c["leaves"], alpha=c["alpha"], eps=c["eps"])
+    buf.update_priorities(torch.from_numpy(c["idx"]).cuda(), torch.from_numpy(c["td"]).cuda())
+    leaves = buf.priorities.cpu().numpy()
+    # last occurrence wins, as in the reference's single-threaded torch backend
+    np.testing.assert_allclose(leaves, g["leaves"], rtol=1e-6, atol=0)
+    np.testing.assert_allclose(buf.block_sums.cpu().numpy(), g["block_sums"], rtol=SUM_RTOL)
+    assert ulps(buf._max_priority.item(), g["max_priority"]).max() <= 2
+    check_tree(buf)
+    assert buf.status()["errors"] == 0
+
+
+def test_add_wraparound_matches_golden():
+    c = cases.case_add_wrap()
+    g = np.load(os.path.join(GOLDEN, "add_wrap.npz"))
+    buf = make_buffer(c["capacity"], c["fields"])
+    steps = [("add", c["adds"][0]), ("upd", None), ("add", c["adds"][1]), ("add", c["adds"][2])]
+    for k, (kind, rows) in enumerate(steps):
+        if kind == "add":
+            buf.add({"x": torch.from_numpy(rows).cuda()})
+        else:
+            buf.update_priorities(torch.from_numpy(c["upd_idx"]).cuda(),
+                                  torch.from_numpy(c["upd_td"]).cuda())
+        np.testing.assert_array_equal(buf.storage.cpu().numpy(), g[f"s{k}_storage"])
+        np.testing.assert_allclose(buf.priorities.cpu().numpy(), g[f"s{k}_leaves"], rtol=1e-6)
+        np.testing.assert_allclose(buf.block_sums.cpu().numpy(), g[f"s{k}_block_sums"],
+                                   rtol=SUM_RTOL)
+        np.testing.assert_array_equal([buf._cursor, buf.size], g[f"s{k}_cursor_size"])
+        np.testing.assert_array_equal(buf._size_cursor.cpu().numpy()[::-1], g[f"s{k}_cursor_size"])
+        check_tree(buf)
+
+
+# ------------------------------------------------------------------ full sizes
+def _leaves(rng, n, kind):
+    if kind == "absnormal":
+        return cases.leaves_abs_normal(rng, n)
+    if kind == "heavy":
+        x = rng.lognormal(0.0, 2.0, n).astype(np.float32)
+        x[rng.choice(n, n // 100, replace=False)] = 0.0
+        return x
+    return rng.lognormal(0.0, 1.0, n).astype(np.float32)
+
+
+@pytest.mark.parametrize("kind,batches", [
+    ("absnormal", [256, 4096]),
+    ("heavy", [32, 128, 512, 2048, 8192, 32768, 65536]),
+])
+def test_full_size_1m_x_74(kind, batches):
+    """1,000,000 x 74 rows: the UTD configuration and the heavy-tailed batch sweep."""
+    rng = np.random.default_rng(11)
+    cap = 1_000_000
+    leaves = _leaves(rng, cap, kind)
+    rows = rng.standard_normal((cap, 74), dtype=np.float32)
+    buf = make_buffer(cap, {"row": 74}, {"row": rows}, leaves)
+    check_tree(buf)
+    for b in batches:
+        rand = rng.random(b, dtype=np.float32)
+        r = check_sample(buf, rows, leaves, cap, rand, 0.4, tag=f"{kind} B={b}")
+        print(f"PARITY 1Mx74 {kind} B={b}: {r}")
+        assert r["excused"] <= max(3, b // 20)
+    st = buf.status()
+    assert st["errors"] == 0 and st["timeouts"] == 0
+
+
+def test_update_storm_full_size():
+    """65,536 indices with 50% duplicates on 1M slots: last occurrence wins,
+    sums exact; repeated storms never drift."""
+    rng = np.random.default_rng(12)
+    cap = 1_000_000
+    leaves = _leaves(rng, cap, "heavy")
+    buf = make_buffer(cap, {"x": 1}, None, leaves)
+    st = oracle.OracleStore(cap, {"x": 1})
+    st.set_priorities(np.pad(leaves, (0, st.capacity_padded - cap)))
+    for it in range(20):
+        half = rng.integers(0, cap, 32768)
+        idx = np.concatenate([half, half[rng.integers(0, 32768, 32768)]])
+        rng.shuffle(idx)
+        td = (rng.standard_normal(idx.size) * 3).astype(np.float32)
+        buf.update_priorities(torch.from_numpy(idx).cuda(), torch.from_numpy(td).cuda())
+        st.update_priorities(idx, td)
+    np.testing.assert_allclose(buf.priorities.cpu().numpy(), st.priorities, rtol=1e-6, atol=0)
+    np.testing.assert_allclose(buf.block_sums.cpu().numpy(), st.block_sums, rtol=SUM_RTOL)
+    assert ulps(buf._max_priority.item(), st.max_priority).max() <= 2
+    check_tree(buf)
+
+
+def test_wide_rows_gather_bit_exact():
+    """row_dim 4096 (16 KB rows, float4 path): rows are bit-exact copies."""
+    rng = np.random.default_rng(13)
+    cap = 20_000
+    rows = rng.random((cap, 4096), dtype=np.float32)
+    leaves = cases.leaves_abs_normal(rng, cap)
+    buf = make_buffer(cap, {"img": 4096}, {"img": rows}, leaves)
+    r = check_sample(buf, rows, leaves, cap, rng.random(1024, dtype=np.float32), 0.6)
+    assert r["equal"] + r["excused"] == 1024
+
+
+@pytest.mark.parametrize("row_dim", [1, 2, 3, 4, 5, 8, 64, 74, 127, 128, 129, 300, 522])
+def test_gather_every_vector_width(row_dim):
+    rng = np.random.default_rng(row_dim)
+    cap = 3000
+    rows = rng.standard_normal((cap, row_dim), dtype=np.float32)
+    leaves = cases.leaves_abs_normal(rng, cap)
+    buf = make_buffer(cap, {"r": row_dim}, {"r": rows}, leaves)
+    check_sample(buf, rows, leaves, cap, rng.random(777, dtype=np.float32), 0.4)
+
+
+# ------------------------------------------------------------------ edge cases
+@pytest.mark.parametrize("cap", [1, 2, 31, 32, 33, 1023, 1024, 1025, 4096 * 32, 4096 * 32 + 1,
+                                 99_991])
+def test_capacities(cap):
+    rng = np.random.default_rng(cap)
+    rows = rng.standard_normal((cap, 3), dtype=np.float32)
+    leaves = _leaves(rng, cap, "absnormal")
+    buf = make_buffer(cap, {"a": 2, "b": 1}, {"a": rows[:, :2], "b": rows[:, 2:]}, leaves)
+    check_tree(buf)
+    check_sample(buf, rows, leaves, cap, rng.random(513, dtype=np.float32), 0.4, tag=str(cap))
+
+
+def test_batch_one_and_batch_larger_than_capacity():
+    rng = np.random.default_rng(21)
+    cap = 100
+    rows = rng.standard_normal((cap, 2), dtype=np.float32)
+    leaves = _leaves(rng, cap, "absnormal")
+    buf = make_buffer(cap, {"x": 2}, {"x": rows}, leaves)
+    check_sample(buf, rows, leaves, cap, rng.random(1, dtype=np.float32), 0.4)
+    check_sample(buf, rows, leaves, cap, rng.random(100_000, dtype=np.float32), 0.4)
+
+
+def test_partial_fill_never_samples_past_size():
+    rng = np.random.default_rng(22)
+    buf = make_buffer(5000, {"x": 1})
+    buf.add({"x": torch.arange(1234, dtype=torch.float32).reshape(-1, 1).cuda()})
+    _, idx, w = buf.sample(65536)
+    assert int(idx.max()) < 1234 and int(idx.min()) >= 0
+    assert torch.isfinite(w).all() and (w > 0).all() and float(w.max()) == 1.0
+    del rng
+
+
+def test_uniform_at_top_of_range_falls_back_to_last_positive_slot():
+    """rand just below 1 can make u round up to the total: the draw takes the
+    last slot with mass and is counted as a fallback, never an empty slot."""
+    cap = 3000
+    leaves = np.ones(cap, np.float32)
+    leaves[2500:] = 0.0
+    buf = make_buffer(cap, {"x": 1}, {"x": np.arange(cap, dtype=np.float32)[:, None]}, leaves)
+    rand = torch.full((64,), np.nextafter(np.float32(1), np.float32(0)), device="cuda")
+    _, idx, w = buf.sample_from_uniforms(rand, 0.4)
+    assert (idx.cpu().numpy() == 2499).all()
+    assert torch.isfinite(w).all()
+
+
+def test_clamped_empty_slot_walks_back():
+    """Mass beyond `size` (written by a caller) clamps to size-1; an empty slot
+    there is replaced by the last positive slot before it and counted."""
+    cap = 2000
+    buf = make_buffer(cap, {"x": 1})
+    buf.add({"x": torch.arange(1000, dtype=torch.float32).reshape(-1, 1).cuda()})
+    lv = np.ones(cap, np.float32)
+    lv[990:] = 0.0
+    lv[1500] = 1e6  # beyond size: every draw lands here and clamps
+    buf.priorities[:cap] = torch.from_numpy(lv).cuda()
+    buf.rebuild_sums()
+    buf.clear_status()
+    _, idx, w = buf.sample(4096)
+    i = idx.cpu().numpy()
+    assert set(np.unique(i)) <= set(range(990))
+    assert torch.isfinite(w).all()
+    st = buf.status()
+    assert st["clamps"] > 0 and st["zero_walks"] > 0
+
+
+def test_bad_update_indices_are_skipped_and_counted():
+    buf = make_buffer(1000, {"x": 1}, {"x": np.zeros((1000, 1), np.float32)})
+    before = buf.priorities.clone()
+    idx = torch.tensor([5, -1, 1000, 10**9, 6], device="cuda")
+    buf.update_priorities(idx, torch.tensor([1.0, 2.0, 3.0, 4.0, 5.0], device="cuda"))
+    after = buf.priorities.cpu().numpy()
+    assert after[5] == pytest.approx((1.0 + 1e-6) ** 0.6, rel=1e-6)
+    assert after[6] == pytest.approx((5.0 + 1e-6) ** 0.6, rel=1e-6)
+    changed = np.nonzero(after != before.cpu().numpy())[0]
+    assert set(changed) == {5, 6}
+    st = buf.status()
+    assert st["bad_indices"] == 3
+    check_tree(buf)
+
+
+def test_empty_and_invalid_calls_raise():
+    buf = make_buffer(100, {"x": 1})
+    with pytest.raises(AssertionError):
+        buf.sample(4)  # reference: assert self.size > 0
+    buf.add({"x": torch.zeros(10, 1, device="cuda")})
+    with pytest.raises(RuntimeError):
+        buf.sample(0)
+    with pytest.raises(RuntimeError):
+        buf.update_priorities(torch.zeros(0, dtype=torch.int64, device="cuda"),
+                              torch.zeros(0, device="cuda"))
+    with pytest.raises(ValueError):
+        buf.update_priorities(torch.zeros(3, dtype=torch.int64, device="cuda"),
+                              torch.zeros(2, device="cuda"))
+    buf.add({"x": torch.zeros(0, 1, device="cuda")})  # empty add is a no-op
+    assert buf.size == 10
+
+
+def test_add_converts_dtypes_and_strided_fields():
+    buf = make_buffer(64, {"a": 3, "d": 1})
+    a = torch.arange(30, dtype=torch.float64).reshape(10, 3).cuda()
+    d = torch.ones(10, dtype=torch.bool).cuda()
+    big = torch.arange(50, dtype=torch.float32).reshape(10, 5).cuda()
+    buf.add({"a": a, "d": d})
+    buf.add({"a": big[:, 1:4], "d": big[:, :1]})  # strided views
+    st = buf.storage.cpu().numpy()
+    np.testing.assert_array_equal(st[:10, :3], a.cpu().numpy())
+    np.testing.assert_array_equal(st[:10, 3], 1.0)
+    np.testing.assert_array_equal(st[10:20, :3], big[:, 1:4].cpu().numpy())
+    np.testing.assert_array_equal(st[10:20, 3], big[:, 0].cpu().numpy())
+    assert buf.size == 20 and buf._size_cursor.tolist() == [20, 20]

@@ -1,0 +1,236 @@
+// extern "C" entry points: argument checks, layout, launch plumbing.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "per_b200.h"
+#include "per_internal.h"
+
+namespace {
+
+thread_local int g_last_cuda = 0;
+
+struct OccEntry {
+  int device;
+  const void* fn;
+  int threads;
+  size_t smem;
+  int ctas;
+};
+constexpr int kOccSlots = 256;
+OccEntry g_occ[kOccSlots];
+int g_occ_n = 0;
+std::mutex g_occ_mu;
+
+bool cooperative_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("PER_COOPERATIVE");
+    v = (s && s[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+PerTree tree_of(const per_store_t* s) {
+  PerTree t;
+  for (int k = 0; k < PER_MAX_LEVELS; ++k) {
+    t.levels[k] = s->levels[k];
+    t.claims[k] = s->claims[k];
+    t.level_len[k] = s->level_len[k];
+  }
+  t.num_levels = s->num_levels;
+  t.top_level = s->top_level;
+  t.capacity = s->capacity;
+  t.storage = s->storage;
+  t.row_dim = s->row_dim;
+  t.row_stride = s->row_stride;
+  t.size_cursor = s->size_cursor;
+  t.max_priority = s->max_priority;
+  t.status = s->status;
+  t.scratch = reinterpret_cast<PerScratch*>(s->scratch);
+  t.alpha = s->alpha;
+  t.eps = s->eps;
+  return t;
+}
+
+// Checks that a store descriptor is self-consistent with per_layout().
+int check_store(const per_store_t* s) {
+  if (!s) return PER_ERR_NULL_POINTER;
+  per_layout_t l;
+  int rc = per_layout(s->capacity, &l);
+  if (rc) return rc;
+  if (s->num_levels != l.num_levels || s->top_level != l.top_level) return PER_ERR_INVALID_ARGUMENT;
+  for (int k = 0; k < l.num_levels; ++k) {
+    if (!s->levels[k] || !s->claims[k]) return PER_ERR_NULL_POINTER;
+    if (s->level_len[k] != l.level_len[k]) return PER_ERR_INVALID_ARGUMENT;
+    if (((uintptr_t)s->levels[k]) % 16) return PER_ERR_MISALIGNED;
+  }
+  if (!s->storage || !s->size_cursor || !s->max_priority || !s->status || !s->scratch)
+    return PER_ERR_NULL_POINTER;
+  if (s->scratch_bytes < PER_SCRATCH_BYTES) return PER_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)s->scratch) % 16 || ((uintptr_t)s->storage) % 4) return PER_ERR_MISALIGNED;
+  if (s->row_dim < 1 || s->row_stride < s->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  if (!(s->eps >= 0.f) || !(s->alpha == s->alpha)) return PER_ERR_INVALID_ARGUMENT;
+  return PER_OK;
+}
+
+}  // namespace
+
+int per_record_cuda(cudaError_t e) {
+  g_last_cuda = (int)e;
+  return PER_ERR_CUDA;
+}
+
+int per_coresident_ctas(const void* fn, int threads, size_t smem, int* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return per_record_cuda(e);
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    for (int i = 0; i < g_occ_n; ++i) {
+      const OccEntry& o = g_occ[i];
+      if (o.device == dev && o.fn == fn && o.threads == threads && o.smem == smem) {
+        *out = o.ctas;
+        return PER_OK;
+      }
+    }
+  }
+  int sms = 0, per_sm = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return per_record_cuda(e);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
+  if (e != cudaSuccess) return per_record_cuda(e);
+  if (per_sm < 1) return PER_ERR_TOO_LARGE;
+  const int ctas = sms * per_sm;
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    if (g_occ_n < kOccSlots) g_occ[g_occ_n++] = OccEntry{dev, fn, threads, smem, ctas};
+  }
+  *out = ctas;
+  return PER_OK;
+}
+
+cudaError_t per_launch(const void* fn, unsigned grid, unsigned threads, size_t smem,
+                       cudaStream_t stream, void** args, bool grid_sync) {
+  bool coop = grid_sync && cooperative_enabled();
+  if (coop) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(stream, &cs);
+    if (e != cudaSuccess) return e;
+    if (cs != cudaStreamCaptureStatusNone) coop = false;
+  }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = coop ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+extern "C" {
+
+int per_abi_version(void) { return PER_ABI_VERSION; }
+
+int per_last_cuda_error(void) { return g_last_cuda; }
+
+const char* per_error_string(int code) {
+  switch (code) {
+    case PER_OK: return "ok";
+    case PER_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PER_ERR_NULL_POINTER: return "null pointer";
+    case PER_ERR_EMPTY: return "empty input";
+    case PER_ERR_TOO_LARGE: return "size exceeds a supported maximum";
+    case PER_ERR_MISALIGNED: return "misaligned pointer or stride";
+    case PER_ERR_CUDA: return "CUDA error (see per_last_cuda_error)";
+    case PER_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown error";
+  }
+}
+
+int per_layout(int64_t capacity, per_layout_t* out) {
+  if (!out) return PER_ERR_NULL_POINTER;
+  if (capacity < 1) return PER_ERR_INVALID_ARGUMENT;
+  if (capacity > ((int64_t)1 << 30)) return PER_ERR_TOO_LARGE;
+  memset(out, 0, sizeof(*out));
+  out->capacity = capacity;
+  out->num_blocks = (capacity + PER_BLOCK_P - 1) / PER_BLOCK_P;
+  out->capacity_padded = out->num_blocks * PER_BLOCK_P;
+  int top = -1;
+  for (int k = 0; k < PER_MAX_LEVELS; ++k) {
+    const int64_t span = (int64_t)1 << (PER_LOG_FANOUT * k);
+    out->level_nodes[k] = (capacity + span - 1) / span;
+    if (top < 0 && k >= 1 && out->level_nodes[k] <= PER_TOP_MAX) top = k;
+  }
+  if (top < 0) return PER_ERR_TOO_LARGE;
+  out->top_level = top;
+  out->num_levels = top + 1 > 3 ? top + 1 : 3;
+  out->level_len[0] = out->capacity_padded;
+  for (int k = 1; k < out->num_levels; ++k)
+    out->level_len[k] = (out->level_nodes[k] + PER_FANOUT - 1) / PER_FANOUT * PER_FANOUT;
+  out->scratch_bytes = PER_SCRATCH_BYTES;
+  return PER_OK;
+}
+
+int per_sample_fused(const per_store_t* store, const float* rand, int64_t batch, float beta,
+                     float* out, int64_t out_stride, int64_t* idx, float* w, void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (!rand || !out || !idx || !w) return PER_ERR_NULL_POINTER;
+  if (batch < 1) return PER_ERR_EMPTY;
+  if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
+  if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4)
+    return PER_ERR_MISALIGNED;
+  return per_launch_sample(tree_of(store), rand, batch, beta, out, out_stride, idx, w,
+                           (cudaStream_t)stream);
+}
+
+int per_update_priorities(const per_store_t* store, const int64_t* idx, const float* td, int64_t n,
+                          void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (!idx || !td) return PER_ERR_NULL_POINTER;
+  if (n < 1) return PER_ERR_EMPTY;
+  if (n >= (int64_t)0xffffffffLL) return PER_ERR_TOO_LARGE;
+  return per_launch_update(tree_of(store), idx, td, n, (cudaStream_t)stream);
+}
+
+int per_add(const per_store_t* store, const per_field_t* fields, int32_t n_fields, int64_t n,
+            void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (n < 0) return PER_ERR_INVALID_ARGUMENT;
+  if (n == 0) return PER_OK;
+  if (!fields) return PER_ERR_NULL_POINTER;
+  if (n_fields < 1 || n_fields > PER_MAX_FIELDS) return PER_ERR_INVALID_ARGUMENT;
+  int64_t covered = 0;
+  for (int f = 0; f < n_fields; ++f) {
+    const per_field_t& fd = fields[f];
+    if (!fd.data) return PER_ERR_NULL_POINTER;
+    if (fd.dim < 1 || fd.stride < fd.dim || fd.col_offset < 0 ||
+        fd.col_offset + fd.dim > store->row_dim)
+      return PER_ERR_INVALID_ARGUMENT;
+    covered += fd.dim;
+  }
+  if (covered != store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  return per_launch_add(tree_of(store), fields, n_fields, n, (cudaStream_t)stream);
+}
+
+int per_rebuild_sums(const per_store_t* store, void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  return per_launch_rebuild(tree_of(store), (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,30 @@
+// Host-side helpers shared by the launchers and the C entry points.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "per_common.cuh"
+
+// Record a CUDA error for per_last_cuda_error() and return PER_ERR_CUDA.
+int per_record_cuda(cudaError_t e);
+
+// Largest grid of `fn` (threads per CTA, dynamic shared bytes) whose CTAs are
+// all co-resident on the current device; cached per (device, fn, smem).
+int per_coresident_ctas(const void* fn, int threads, size_t smem, int* out);
+
+// Launch `fn`. With grid_sync the CTAs wait on one another through
+// PerGridBarrier, so the grid must not exceed per_coresident_ctas(); the
+// launch then asks for co-scheduling (cooperative attribute) unless the
+// stream is being captured into a graph.
+cudaError_t per_launch(const void* fn, unsigned grid, unsigned threads, size_t smem,
+                       cudaStream_t stream, void** args, bool grid_sync);
+
+int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float beta,
+                      float* out, int64_t out_stride, int64_t* idx, float* w,
+                      cudaStream_t stream);
+int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int64_t n,
+                      cudaStream_t stream);
+int per_launch_add(const PerTree& t, const per_field_t* fields, int32_t n_fields, int64_t n,
+                   cudaStream_t stream);
+int per_launch_rebuild(const PerTree& t, cudaStream_t stream);

@@ -1,0 +1,201 @@
+"""GPU-resident prioritized replay buffer on hand-written sm_100a kernels.
+
+Drop-in for triton-per's `PERBuffer` with its `triton` backend
+(src/triton_per/buffer.py:23-162): same constructor, attributes, `add`,
+`sample(batch_size, beta) -> (views, idx, w)` and
+`update_priorities(indices, td_errors)`, and the module constant BLOCK_P.
+
+Storage is one packed float32[capacity, row_dim] tensor and sampling returns
+zero-copy field views of a freshly allocated [batch, row_dim] output, as in the
+reference. Priorities live in the reference's two-level store (leaves padded
+to BLOCK_P per block plus float32 block sums), widened into a 32-ary sum tree:
+the engine also keeps 32-leaf chunk sums (and, above 4M slots, sums of 32
+blocks) so that every level of a search is one coalesced warp load.
+
+Every call enqueues CUDA work on the current stream and returns without a host
+synchronisation (the reference's add() synchronises through torch.unique; this
+one does not). There is no CPU path: a non-CUDA device raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+BLOCK_P = 1024  # priorities per block (reference buffer.py:20)
+
+_BACKENDS = ("triton", "triton-unfused", "b200")
+
+
+def _stream_ptr(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+class PERBuffer:
+    def __init__(
+        self,
+        capacity: int,
+        fields: dict[str, int],  # name -> flattened per-transition dim
+        device: str | torch.device = "cuda",
+        alpha: float = 0.6,
+        eps: float = 1e-6,
+        backend: str = "triton",
+    ):
+        assert backend in _BACKENDS, (
+            f"backend {backend!r}: this engine replaces the reference's triton backends; "
+            f"use one of {_BACKENDS}")
+        self.capacity = capacity
+        self.fields = dict(fields)
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("per_b200.PERBuffer runs on CUDA devices only (no CPU fallback)")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.alpha = alpha
+        self.eps = eps
+        self.backend = backend
+
+        self.row_dim = sum(fields.values())
+        self._offsets: dict[str, tuple[int, int]] = {}
+        o = 0
+        for name, d in fields.items():
+            self._offsets[name] = (o, o + d)
+            o += d
+
+        lay = _lib.layout(capacity)
+        self._layout = lay
+        self.num_blocks = int(lay.num_blocks)
+        self.capacity_padded = int(lay.capacity_padded)
+        self.log2_blocks = max(1, math.ceil(math.log2(self.num_blocks))) if self.num_blocks > 1 else 0
+        self.num_levels = int(lay.num_levels)
+        self.top_level = int(lay.top_level)
+
+        dev = self.device
+        self.storage = torch.zeros(capacity, self.row_dim, device=dev)
+        self._levels = [torch.zeros(int(lay.level_len[k]), device=dev)
+                        for k in range(self.num_levels)]
+        self.priorities = self._levels[0]
+        self.block_sums = self._levels[2][: self.num_blocks]
+        self._claims = [torch.zeros(int(lay.level_len[k]), dtype=torch.int32, device=dev)
+                        for k in range(self.num_levels)]
+        self._size_cursor = torch.zeros(2, dtype=torch.int64, device=dev)
+        # device scalar (already ^alpha space) so updates never sync the host
+        self._max_priority = torch.ones((), device=dev)
+        self._status = torch.zeros(_lib.STATUS_WORDS, dtype=torch.int32, device=dev)
+        self._scratch = torch.zeros(int(lay.scratch_bytes), dtype=torch.uint8, device=dev)
+
+        self.size = 0
+        self._cursor = 0
+
+        s = _lib.Store()
+        for k in range(self.num_levels):
+            s.levels[k] = self._levels[k].data_ptr()
+            s.claims[k] = self._claims[k].data_ptr()
+            s.level_len[k] = int(lay.level_len[k])
+        s.num_levels = self.num_levels
+        s.top_level = self.top_level
+        s.capacity = capacity
+        s.storage = self.storage.data_ptr()
+        s.row_dim = self.row_dim
+        s.row_stride = self.row_dim
+        s.size_cursor = self._size_cursor.data_ptr()
+        s.max_priority = self._max_priority.data_ptr()
+        s.status = self._status.data_ptr()
+        s.scratch = self._scratch.data_ptr()
+        s.scratch_bytes = int(lay.scratch_bytes)
+        s.alpha = float(alpha)
+        s.eps = float(eps)
+        self._store = s
+        self._store_ref = ctypes.byref(s)
+
+    # ------------------------------------------------------------------ add
+    def add(self, batch: dict[str, torch.Tensor]) -> None:
+        """Insert a batch of transitions (new entries get max priority)."""
+        n = next(iter(batch.values())).shape[0]
+        if n == 0:
+            return
+        keep = []
+        fields = (_lib.Field * len(self._offsets))()
+        for f, (name, (a, b)) in enumerate(self._offsets.items()):
+            t = batch[name].reshape(n, -1)
+            if t.shape[1] != b - a:
+                raise ValueError(f"field {name!r}: expected {b - a} values per row, got {t.shape[1]}")
+            t = t.to(device=self.device, dtype=torch.float32)
+            if t.stride(1) != 1 or t.stride(0) < t.shape[1]:
+                t = t.contiguous()
+            keep.append(t)
+            fields[f].data = t.data_ptr()
+            fields[f].dim = b - a
+            fields[f].stride = t.stride(0)
+            fields[f].col_offset = a
+        with torch.cuda.device(self.device):
+            _lib.check("per_add", _lib.lib.per_add(self._store_ref, fields, len(self._offsets), n,
+                                                   _stream_ptr(self.device)))
+        self._cursor = int((self._cursor + n) % self.capacity)
+        self.size = min(self.size + n, self.capacity)
+
+    # --------------------------------------------------------------- sample
+    def sample(self, batch_size: int, beta: float = 0.4):
+        """Returns (fields: dict of views, indices, normalized IS weights)."""
+        assert self.size > 0
+        rand = torch.rand(batch_size, device=self.device)
+        return self.sample_from_uniforms(rand, beta)
+
+    def sample_from_uniforms(self, rand: torch.Tensor, beta: float = 0.4):
+        """sample() with caller-provided uniforms in [0, 1) (float32, on the device)."""
+        assert self.size > 0
+        if rand.dtype != torch.float32 or rand.device != self.device or not rand.is_contiguous():
+            rand = rand.to(device=self.device, dtype=torch.float32).contiguous()
+        batch_size = rand.numel()
+        out = torch.empty(batch_size, self.row_dim, device=self.device)
+        idx = torch.empty(batch_size, dtype=torch.int64, device=self.device)
+        w = torch.empty(batch_size, device=self.device)
+        with torch.cuda.device(self.device):
+            _lib.check("per_sample_fused", _lib.lib.per_sample_fused(
+                self._store_ref, rand.data_ptr(), batch_size, float(beta), out.data_ptr(),
+                self.row_dim, idx.data_ptr(), w.data_ptr(), _stream_ptr(self.device)))
+        views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
+        return views, idx, w
+
+    # --------------------------------------------------------------- update
+    def update_priorities(self, indices: torch.Tensor, td_errors: torch.Tensor) -> None:
+        td = td_errors.detach().reshape(-1)
+        if td.dtype != torch.float32 or td.device != self.device or not td.is_contiguous():
+            td = td.to(device=self.device, dtype=torch.float32).contiguous()
+        idx = indices.reshape(-1)
+        if idx.dtype != torch.int64 or idx.device != self.device or not idx.is_contiguous():
+            idx = idx.to(device=self.device, dtype=torch.int64).contiguous()
+        if idx.numel() != td.numel():
+            raise ValueError(f"{idx.numel()} indices but {td.numel()} TD errors")
+        with torch.cuda.device(self.device):
+            _lib.check("per_update_priorities", _lib.lib.per_update_priorities(
+                self._store_ref, idx.data_ptr(), td.data_ptr(), idx.numel(),
+                _stream_ptr(self.device)))
+
+    # ------------------------------------------------------------ utilities
+    def rebuild_sums(self) -> None:
+        """Recompute every sum level from the leaves (after writing priorities directly)."""
+        with torch.cuda.device(self.device):
+            _lib.check("per_rebuild_sums", _lib.lib.per_rebuild_sums(
+                self._store_ref, _stream_ptr(self.device)))
+
+    def status(self) -> dict[str, int]:
+        """Device event counters (synchronises the host)."""
+        v = self._status.cpu().tolist()
+        return {name: int(v[k]) & 0xFFFFFFFF for k, name in enumerate(_lib.STATUS_NAMES)}
+
+    def clear_status(self) -> None:
+        self._status.zero_()
+
+    def recover(self) -> None:
+        """Reset the grid-barrier scratch and rebuild the sums after a reported timeout."""
+        self._scratch.zero_()
+        self.rebuild_sums()
+
+    def level(self, k: int) -> torch.Tensor:
+        """Sums at tree level k (0 = leaves, 1 = 32-leaf chunks, 2 = block sums)."""
+        return self._levels[k]
