@@ -405,8 +405,25 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernel-only", type=int, default=0, metavar="BATCH",
+                    help="profiling aid: eager fused samples of this batch (then updates of 256) "
+                         "on the 1M x 74 store, no timing output")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+
+    if args.kernel_only:
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        buf = make_store(dev, seed=1)
+        g = torch.Generator(device=dev).manual_seed(2)
+        for _ in range(args.warmup + args.steps):
+            r = torch.rand(args.kernel_only, generator=g, device=dev)
+            _, idx, _ = buf.sample_from_uniforms(r, BETA)
+            buf.update_priorities(idx[:BATCH], torch.rand(min(BATCH, idx.numel()), device=dev))
+        torch.cuda.synchronize()
+        st = buf.status()
+        print(json.dumps({"kernel_only": args.kernel_only, "status": st}))
+        return
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -119,6 +119,13 @@ typedef struct per_field {
   int64_t col_offset;  /* first column of this field inside a storage row */
 } per_field_t;
 
+/* Storage row stride (elements) the engine recommends for rows of
+ * `row_dim` float32 values: a multiple of 4 (16-byte rows, so rows can be
+ * copied by the Tensor Memory Accelerator) and, when it costs at most 1/8
+ * more memory, of 16 (64-byte rows, fewer DRAM lines per row).
+ * Replaces the packed row layout of reference buffer.py:41,52. */
+int64_t per_row_stride(int64_t row_dim);
+
 /* Fill `out` with the array sizes for a store of `capacity` slots.
  * Replaces the sizing in reference buffer.py:48-54. */
 int per_layout(int64_t capacity, per_layout_t* out);

@@ -113,6 +113,31 @@ int per_coresident_ctas(const void* fn, int threads, size_t smem, int* out) {
   return PER_OK;
 }
 
+int per_set_smem(const void* fn, size_t smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return per_record_cuda(e);
+  static std::mutex mu;
+  static struct {
+    int device;
+    const void* fn;
+    size_t smem;
+  } done[64];
+  static int n_done = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < n_done; ++i)
+    if (done[i].device == dev && done[i].fn == fn && done[i].smem >= smem) return PER_OK;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return per_record_cuda(e);
+  for (int i = 0; i < n_done; ++i)
+    if (done[i].device == dev && done[i].fn == fn) {
+      done[i].smem = smem;
+      return PER_OK;
+    }
+  if (n_done < 64) done[n_done++] = {dev, fn, smem};
+  return PER_OK;
+}
+
 cudaError_t per_launch(const void* fn, unsigned grid, unsigned threads, size_t smem,
                        cudaStream_t stream, void** args, bool grid_sync) {
   bool coop = grid_sync && cooperative_enabled();
@@ -156,6 +181,14 @@ const char* per_error_string(int code) {
     case PER_ERR_NO_DEVICE: return "no CUDA device";
     default: return "unknown error";
   }
+}
+
+int64_t per_row_stride(int64_t row_dim) {
+  if (row_dim < 1) return 0;
+  if (row_dim < 4) return row_dim;
+  const int64_t s16 = (row_dim + 15) / 16 * 16;
+  if ((s16 - row_dim) * 8 <= row_dim) return s16;
+  return (row_dim + 3) / 4 * 4;
 }
 
 int per_layout(int64_t capacity, per_layout_t* out) {

@@ -9,18 +9,20 @@
 
 #define PER_FULL_MASK 0xffffffffu
 
-// Spin limit of every wait: about 2^22 polls with a 256 ns back-off, i.e.
-// on the order of one second before the wait gives up and reports
-// PER_EVT_BARRIER_TIMEOUT instead of hanging the GPU.
+// Spin limit of every wait: 2^22 polls (each an L2 round trip plus a short
+// back-off), i.e. on the order of a second before the wait gives up and
+// reports PER_EVT_BARRIER_TIMEOUT instead of hanging the GPU.
 #define PER_SPIN_LIMIT (1u << 22)
-#define PER_SPIN_SLEEP_NS 256
+#define PER_SPIN_SLEEP_NS 32
 
 // Layout of store->scratch (PER_SCRATCH_BYTES).
 struct PerScratch {
-  uint32_t bar_count;  // arrivals at the current grid barrier
-  uint32_t bar_gen;    // generation, bumped by the last arriver
-  float gmax;          // value published by the last arriver
-  uint32_t pad[61];    // keep partial[] 256-byte aligned
+  uint32_t bar_count;    // arrivals at the current grid barrier
+  uint32_t bar_gen;      // generation, bumped by the last arriver
+  uint32_t mx_count;     // sample: warps that published their max weight
+  uint32_t mx_gen;       // sample: generation, bumped when every warp has published
+  uint32_t mx_bits[2];   // sample: running max weight bits, by generation parity
+  uint32_t pad[58];      // keep partial[] 256-byte aligned
   float partial[PER_MAX_GRID];
 };
 static_assert(sizeof(PerScratch) == PER_SCRATCH_BYTES, "scratch layout");
@@ -41,6 +43,19 @@ __device__ __forceinline__ float per_ld_relaxed_f32(const float* p) {
   return v;
 }
 
+__device__ __forceinline__ uint32_t per_ld_relaxed_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// atomic add with acquire-release semantics at GPU scope; returns the old value
+__device__ __forceinline__ uint32_t per_atom_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void per_count(uint32_t* status, int word, uint32_t n = 1) {
   if (status) atomicAdd(status + word, n);
 }
@@ -53,6 +68,10 @@ __device__ __forceinline__ void per_flag(uint32_t* status, uint32_t bit) {
 // values (and +inf / positive NaN, which sort above) is an integer max.
 __device__ __forceinline__ void per_atomic_max_pos(float* addr, float v) {
   atomicMax(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
+__device__ __forceinline__ uint32_t per_smem_addr_generic(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
 }
 
 // Inclusive warp scan in float64.
@@ -143,21 +162,148 @@ struct PerTree {
   float eps;
 };
 
-// Sum of the 32 children [32*node, 32*node+32) of level `lvl`, in float64,
-// in a fixed order (deterministic). Loads bypass L1 because the children may
-// have been written by other CTAs earlier in the same launch.
-__device__ __forceinline__ double per_sum32(const float* lvl, int64_t node) {
-  const float4* p = reinterpret_cast<const float4*>(lvl + node * PER_FANOUT);
-  float4 q[8];
+// ---- node recomputation (the single definition of a node value)
+//
+// A node's value is the float32 rounding of the float64 sum of its 32
+// children taken as a balanced tree in "butterfly" order: children i and
+// i+16 first, then pairs 8 apart, 4, 2, 1. Every writer of the tree (update,
+// add, rebuild) uses per_sum32_tree below, so a node always has the same bits
+// whichever kernel wrote it.
+__device__ __forceinline__ float per_sum32_tree(const float* c) {
+  double p[16];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) q[i] = __ldcg(p + i);
-  double s = 0.0;
+  for (int i = 0; i < 16; ++i) p[i] = (double)c[i] + (double)c[i + 16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] += p[i + 8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] += p[i + 4];
+  p[0] += p[2];
+  p[1] += p[3];
+  return __double2float_rn(p[0] + p[1]);
+}
+
+constexpr int PER_LINE_STRIDE = 144;                       // staged 128-byte line + 16 (no bank conflicts)
+constexpr int PER_NODE_LINES = 32 * PER_LINE_STRIDE;       // 32 staged lines
+constexpr int PER_NODE_TILE = PER_NODE_LINES + 32 * 8;     // + the warp's node list
+
+__device__ __forceinline__ void per_cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+
+__device__ __forceinline__ void per_cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Stage the 32-child lines of up to 32 nodes into `tile` (one per warp,
+// PER_NODE_TILE bytes): line d holds the children of node nd(d). `node_of(d)`
+// must be callable by every lane for d in [0, 32) (warp-uniform use of
+// shuffles inside is allowed). 4 lines per cp.async instruction, coalesced.
+// Loads bypass L1 (cp.async.cg): children may come from other CTAs of the launch.
+template <typename NodeOf>
+__device__ __forceinline__ void per_stage_lines(const float* child, unsigned char* tile, int cnt,
+                                                int lane, NodeOf node_of) {
+  const uint32_t base = per_smem_addr_generic(tile);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    s += (double)q[i].x;
-    s += (double)q[i].y;
-    s += (double)q[i].z;
-    s += (double)q[i].w;
+    const int q = i * 32 + lane;
+    const int d = q >> 3, part = q & 7;
+    const int64_t nd = node_of(d);
+    if (d < cnt)
+      per_cp_async16(base + (uint32_t)(d * PER_LINE_STRIDE + part * 16),
+                     child + nd * PER_FANOUT + part * 4);
   }
-  return s;
+  per_cp_async_wait_all();
+  __syncwarp();
+}
+
+// Recompute node[l] of level `lvl` from level `child` for every lane whose
+// `own` is set: the owners' lines are staged together (one L2 round trip for
+// up to 32 nodes), then each owner sums its own line.
+__device__ __forceinline__ void per_warp_recompute(const float* child, float* lvl, int64_t node,
+                                                   bool own, int lane, unsigned char* tile) {
+  const uint32_t m = __ballot_sync(PER_FULL_MASK, own);
+  if (!m) return;
+  const int cnt = __popc(m);
+  const int rank = __popc(m & ((1u << lane) - 1u));
+  int64_t* list = reinterpret_cast<int64_t*>(tile + PER_NODE_LINES);
+  if (own) list[rank] = node;
+  __syncwarp();
+  per_stage_lines(child, tile, cnt, lane, [&](int d) { return d < cnt ? list[d] : (int64_t)0; });
+  if (own) {
+    const float4* row = reinterpret_cast<const float4*>(tile + rank * PER_LINE_STRIDE);
+    float c[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = row[i];
+      c[4 * i] = v.x;
+      c[4 * i + 1] = v.y;
+      c[4 * i + 2] = v.z;
+      c[4 * i + 3] = v.w;
+    }
+    lvl[node] = per_sum32_tree(c);
+  }
+  __syncwarp();
+}
+
+// ---- Tensor Memory Accelerator bulk copies (no multicast) and mbarriers
+__device__ __forceinline__ uint32_t per_smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void per_mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(per_smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void per_fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void per_mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(per_smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool per_mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(per_smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for phase `parity` of an mbarrier; false (and a flagged
+// timeout) if it did not complete within the spin limit.
+__device__ __forceinline__ bool per_mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  uint32_t it = 0;
+  while (!per_mbar_try_wait(bar, parity)) {
+    if (++it > PER_SPIN_LIMIT) {
+      per_flag(status, PER_EVT_BARRIER_TIMEOUT);
+      per_count(status, PER_STATUS_TIMEOUTS);
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
+
+// Order earlier generic-proxy shared-memory accesses before later
+// async-proxy (bulk copy) writes to the same shared memory.
+__device__ __forceinline__ void per_fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Bulk copy global -> this CTA's shared memory, completing on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void per_bulk_load(void* sdst, const void* gsrc, uint32_t bytes,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          per_smem_addr(sdst)),
+      "l"(gsrc), "r"(bytes), "r"(per_smem_addr(bar))
+      : "memory");
 }

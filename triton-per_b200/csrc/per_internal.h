@@ -13,6 +13,11 @@ int per_record_cuda(cudaError_t e);
 // all co-resident on the current device; cached per (device, fn, smem).
 int per_coresident_ctas(const void* fn, int threads, size_t smem, int* out);
 
+// Allow `fn` to use up to `smem` bytes of dynamic shared memory on the
+// current device (needed whenever static + dynamic exceeds 48 KB); cached per
+// (device, fn).
+int per_set_smem(const void* fn, size_t smem);
+
 // Launch `fn`. With grid_sync the CTAs wait on one another through
 // PerGridBarrier, so the grid must not exceed per_coresident_ctas(); the
 // launch then asks for co-scheduling (cooperative attribute) unless the

@@ -10,18 +10,26 @@
 //   fused.py:45-52        row copy storage[idx] -> out[j]
 //   buffer.py:92          w / w.max()
 //
-// Design:
+// Design (one draw per lane, 32 draws in flight per warp):
 //   * Prologue: each CTA stages the float64 exclusive prefix of the top tree
-//     level (<= PER_TOP_MAX float32 nodes) in shared memory.
-//   * Search: a warp owns DPW draws at a time. The top level is searched
-//     32-ary with ballots over shared memory; every lower level is one
-//     coalesced 128-byte warp load of the 32 children, a float64 warp scan
-//     and a ballot. The loads of the DPW draws are issued back to back so
-//     their L2 latencies overlap.
+//     level (<= PER_TOP_MAX float32 nodes) in shared memory, padded one slot
+//     in 33 so that the power-of-two strides of a binary search spread over
+//     the banks; every lane then searches it for its own draw.
+//   * Each lower level: the warp copies the 32 children (one 128-byte line)
+//     of each of its 32 draws into a shared-memory tile with cp.async (4
+//     lines per instruction), then every lane searches the 32 children of its
+//     own draw: quad sums, prefix over the 8 quads, then inside the quad.
 //   * Arrive: the CTA publishes the max of its unnormalised weights and
-//     arrives at a grid barrier, then gathers its rows (the HBM-bound part)
-//     while the other CTAs finish, then waits, reads the global max and
-//     normalises its weights.
+//     arrives at a grid barrier, then gathers its rows while the other CTAs
+//     finish, then waits, reads the global max and normalises its weights.
+//   * Gather: every lane issues one Tensor Memory Accelerator bulk copy of
+//     its row (16-byte aligned storage rows) into the warp's tile, completing
+//     on the warp's mbarrier; the warp then writes the contiguous output rows
+//     with coalesced vector stores. The bulk engine keeps far more row reads
+//     in flight per SM than per-thread loads can. Rows that are not 16-byte
+//     aligned use cp.async; rows wider than the tile are copied directly.
+//   * Small batches use one-warp CTAs so that their rows are fetched by many
+//     SMs at once; large batches use 8-warp CTAs.
 // Sampling semantics: idx is the first slot whose inclusive prefix exceeds
 // u = rand * total (fp32 product, as torch computes it), with prefixes in
 // float64 so the result equals a search over exact prefixes; rounding
@@ -33,10 +41,113 @@
 
 namespace {
 
-constexpr int kSampleThreads = 256;
-constexpr int kDPW = 4;           // draws per warp in flight
-constexpr int kSegVec = 64;       // vectors per gather segment (2 per lane)
-constexpr int kGatherUnroll = 4;  // segments per warp in flight
+constexpr int kMaxWarps = 8;
+constexpr int kStageMin = PER_NODE_TILE;
+constexpr int kStageMax = 10240;  // per-warp staging bytes for row gathers
+
+struct SampleArgs {
+  PerTree t;
+  const float* rand;
+  int64_t batch;
+  float beta;
+  float* out;
+  int64_t out_stride;
+  int64_t* idx;
+  float* w;
+  int32_t nvec;            // vectors per row
+  int32_t rows_per_stage;  // rows per staged batch (0: wide rows, direct copy)
+  int32_t stage_bytes;     // per-warp staging bytes
+  int32_t row_bytes;       // staged bytes per row (bulk: row_dim*4 rounded up to 16)
+  int32_t use_bulk;        // rows are 16-byte aligned: gather with bulk copies
+  int32_t pre_bytes;       // bytes of the padded prefix array
+  int64_t num_tiles;
+};
+
+// Padded position of prefix entry i: one spare double every 32.
+__device__ __forceinline__ int ppos(int i) { return i + (i >> 5); }
+
+// Number of k in [1, n] with pre[k] <= t, i.e. the first node whose inclusive
+// prefix exceeds t (n if none). Branch-free binary lifting, per lane.
+__device__ __forceinline__ int upper_bound_pre(const double* pre, int n, double t) {
+  int pos = 0;
+  for (int step = 1 << (31 - __clz(n)); step > 0; step >>= 1) {
+    const int np = pos + step;
+    pos = (np <= n && pre[ppos(np)] <= t) ? np : pos;
+  }
+  return pos;
+}
+
+// Number of k in [1, n] with pre[k] < t: the first node whose inclusive prefix
+// reaches t (n if none).
+__device__ __forceinline__ int lower_bound_pre(const double* pre, int n, double t) {
+  int pos = 0;
+  for (int step = 1 << (31 - __clz(n)); step > 0; step >>= 1) {
+    const int np = pos + step;
+    pos = (np <= n && pre[ppos(np)] < t) ? np : pos;
+  }
+  return pos;
+}
+
+// Search the 32 children c[] of a node for the first whose inclusive prefix
+// exceeds r. Returns the child f, its exclusive prefix *ex and value *val;
+// *fb is set when rounding left r at or past the node's sum (then the last
+// positive child is taken).
+__device__ __forceinline__ int search32(const float* c, double r, double* ex, float* val,
+                                       bool* fb) {
+  double q[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    q[k] = ((double)c[4 * k] + (double)c[4 * k + 1]) + ((double)c[4 * k + 2] + (double)c[4 * k + 3]);
+  double pre = 0.0, base = 0.0, lbase = 0.0;
+  int kq = -1, lq = -1;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const double np = pre + q[k];
+    if (kq < 0 && np > r) {
+      kq = k;
+      base = pre;
+    }
+    if (q[k] > 0.0) {
+      lq = k;
+      lbase = pre;
+    }
+    pre = np;
+  }
+  bool last = false;
+  if (kq < 0) {  // past the node's sum: the last quad with mass
+    *fb = true;
+    last = true;
+    kq = lq < 0 ? 0 : lq;
+    base = lq < 0 ? 0.0 : lbase;
+  }
+  float e0 = c[0], e1 = c[1], e2 = c[2], e3 = c[3];
+#pragma unroll
+  for (int k = 1; k < 8; ++k)
+    if (k == kq) {
+      e0 = c[4 * k];
+      e1 = c[4 * k + 1];
+      e2 = c[4 * k + 2];
+      e3 = c[4 * k + 3];
+    }
+  const double s1 = base + (double)e0, s2 = s1 + (double)e1, s3 = s2 + (double)e2;
+  const double s4 = s3 + (double)e3;
+  int j;
+  if (!last && s1 > r) {
+    j = 0;
+  } else if (!last && s2 > r) {
+    j = 1;
+  } else if (!last && s3 > r) {
+    j = 2;
+  } else if (!last && s4 > r) {
+    j = 3;
+  } else {  // last positive element of the quad
+    if (!last) *fb = true;
+    j = e3 > 0.f ? 3 : e2 > 0.f ? 2 : e1 > 0.f ? 1 : 0;
+  }
+  *ex = j == 0 ? base : j == 1 ? s1 : j == 2 ? s2 : s3;
+  *val = j == 0 ? e0 : j == 1 ? e1 : j == 2 ? e2 : e3;
+  return 4 * kq + j;
+}
 
 template <int VEC>
 struct VecT;
@@ -53,306 +164,405 @@ struct VecT<1> {
   using T = float;
 };
 
-struct SampleArgs {
-  PerTree t;
-  const float* rand;
-  int64_t batch;
-  float beta;
-  float* out;
-  int64_t out_stride;
-  int64_t* idx;
-  float* w;
-  int64_t draws_per_cta;
-  int32_t nvec;  // vectors per row
-  int32_t nseg;  // gather segments per row
-};
-
-// First k in [0, n) with pre[k + 1] > t (upper bound over the inclusive
-// prefixes), or n if none. Warp-cooperative, 32-ary; pre is in shared memory.
-__device__ __forceinline__ int top_upper_bound(const double* pre, int n, double t, int lane) {
-  int lo = 0, len = n;
-  while (len > 32) {
-    const int step = (len + 31) >> 5;
-    const int q = lo + min((lane + 1) * step, len) - 1;
-    const uint32_t m = __ballot_sync(PER_FULL_MASK, pre[q + 1] > t);
-    if (!m) return lo + len;
-    const int f = __ffs(m) - 1;
-    lo += f * step;
-    len = min(step, len - f * step);
-  }
-  const uint32_t m = __ballot_sync(PER_FULL_MASK, lane < len && pre[lo + lane + 1] > t);
-  return m ? lo + __ffs(m) - 1 : lo + len;
+__device__ __forceinline__ void cp_async(uint32_t saddr, const void* g, int bytes) {
+  if (bytes == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+  else if (bytes == 8)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(saddr), "l"(g) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(saddr), "l"(g) : "memory");
 }
 
-// First k in [0, n) with pre[k + 1] >= t, or n if none.
-__device__ __forceinline__ int top_lower_bound(const double* pre, int n, double t, int lane) {
-  int lo = 0, len = n;
-  while (len > 32) {
-    const int step = (len + 31) >> 5;
-    const int q = lo + min((lane + 1) * step, len) - 1;
-    const uint32_t m = __ballot_sync(PER_FULL_MASK, pre[q + 1] >= t);
-    if (!m) return lo + len;
-    const int f = __ffs(m) - 1;
-    lo += f * step;
-    len = min(step, len - f * step);
+// Store staged rows (row r at r * spitch vectors) to out rows j0 + r, as one
+// flat lane-strided walk over all vectors (coalesced stores).
+template <int VEC>
+__device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stage, int spitch,
+                                           int64_t j0, int rn, int lane) {
+  using V = typename VecT<VEC>::T;
+  const int nvec = a.nvec;
+  const V* sv = reinterpret_cast<const V*>(stage);
+  V* dst = reinterpret_cast<V*>(a.out) + j0 * (a.out_stride / VEC);
+  const int dstride = (int)(a.out_stride / VEC);
+  const int pieces = rn * nvec;
+  if (nvec >= 32) {  // at most one row wrap per step of 32
+    int r = 0, c = lane;
+    if (c >= nvec) {
+      c -= nvec;
+      ++r;
+    }
+    for (int p = lane; p < pieces; p += 32) {
+      dst[r * dstride + c] = sv[r * spitch + c];
+      c += 32;
+      if (c >= nvec) {
+        c -= nvec;
+        ++r;
+      }
+    }
+  } else {
+    for (int p = lane; p < pieces; p += 32) {
+      const int r = p / nvec, c = p - r * nvec;
+      dst[r * dstride + c] = sv[r * spitch + c];
+    }
   }
-  const uint32_t m = __ballot_sync(PER_FULL_MASK, lane < len && pre[lo + lane + 1] >= t);
-  return m ? lo + __ffs(m) - 1 : lo + len;
+}
+
+// Rows through shared memory with cp.async: lowest latency for a few rows
+// per SM (rows at any 4-byte alignment).
+template <int VEC>
+__device__ __forceinline__ void gather_staged(const SampleArgs& a, unsigned char* stage,
+                                              const int32_t* s_idx, int64_t j0, int nrows,
+                                              int lane) {
+  using V = typename VecT<VEC>::T;
+  const int nvec = a.nvec;
+  const uint32_t sbase = per_smem_addr(stage);
+  const V* src = reinterpret_cast<const V*>(a.t.storage);
+  const int64_t sstride = a.t.row_stride / VEC;
+  for (int r0 = 0; r0 < nrows; r0 += a.rows_per_stage) {
+    const int rn = min(a.rows_per_stage, nrows - r0);
+    const int pieces = rn * nvec;
+    for (int p = lane; p < pieces; p += 32) {
+      const int r = p / nvec, c = p - r * nvec;
+      cp_async(sbase + (uint32_t)(p * VEC * 4), src + (int64_t)s_idx[r0 + r] * sstride + c, VEC * 4);
+    }
+    per_cp_async_wait_all();
+    __syncwarp();
+    store_rows<VEC>(a, stage, nvec, j0 + r0, rn, lane);
+    __syncwarp();
+  }
+}
+
+// Rows through shared memory with one bulk copy per lane (16-byte aligned rows).
+template <int VEC>
+__device__ __forceinline__ void gather_bulk(const SampleArgs& a, unsigned char* stage,
+                                            const int32_t* s_idx, int64_t j0, int nrows,
+                                            int lane, uint64_t* mbar, uint32_t& phase) {
+  const float* src = a.t.storage;
+  for (int r0 = 0; r0 < nrows; r0 += a.rows_per_stage) {
+    const int rn = min(a.rows_per_stage, nrows - r0);
+    per_fence_proxy_async_smem();  // earlier generic accesses of the tile before the bulk writes
+    __syncwarp();
+    if (lane == 0) per_mbar_arrive_expect_tx(mbar, (uint32_t)(rn * a.row_bytes));
+    __syncwarp();
+    if (lane < rn)
+      per_bulk_load(stage + lane * a.row_bytes, src + (int64_t)s_idx[r0 + lane] * a.t.row_stride,
+                    (uint32_t)a.row_bytes, mbar);
+    per_mbar_wait(mbar, phase, a.t.status);
+    phase ^= 1u;
+    store_rows<VEC>(a, stage, a.row_bytes / (VEC * 4), j0 + r0, rn, lane);
+    __syncwarp();
+  }
+}
+
+// Wide rows: each row copied directly by the whole warp, 8 vectors per lane in flight.
+template <int VEC>
+__device__ __forceinline__ void gather_direct(const SampleArgs& a, const int32_t* s_idx,
+                                              int64_t j0, int nrows, int lane) {
+  using V = typename VecT<VEC>::T;
+  const int nvec = a.nvec;
+  const V* src = reinterpret_cast<const V*>(a.t.storage);
+  V* dst = reinterpret_cast<V*>(a.out);
+  const int64_t sstride = a.t.row_stride / VEC;
+  const int64_t dstride = a.out_stride / VEC;
+  constexpr int U = 8;
+  for (int r = 0; r < nrows; ++r) {
+    const V* s = src + (int64_t)s_idx[r] * sstride;
+    V* d = dst + (j0 + r) * dstride;
+    for (int c0 = 0; c0 < nvec; c0 += 32 * U) {
+      V buf[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < nvec) buf[u] = __ldcs(s + c);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < nvec) d[c] = buf[u];
+      }
+    }
+  }
 }
 
 template <int VEC>
-__global__ void __launch_bounds__(kSampleThreads) per_sample_kernel(SampleArgs a) {
-  extern __shared__ double s_pre[];  // [n_top + 1]
-  __shared__ double s_wsum[32];
-  __shared__ uint32_t s_max_bits;
-  __shared__ int s_last;
-  __shared__ float s_gmax;
+__global__ void __launch_bounds__(kMaxWarps * 32) per_sample_kernel(SampleArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ double s_wsum[kMaxWarps];
+  __shared__ int32_t s_rows[kMaxWarps][32];
+  __shared__ uint64_t s_mbar[kMaxWarps];
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
+  const int nthreads = blockDim.x;
+  const int64_t tile_draws = nthreads;
   const PerTree& t = a.t;
+  PerScratch* sc = t.scratch;
+  const int top = t.top_level;
+  const int n_top = (int)t.level_len[top];
+  double* s_pre = reinterpret_cast<double*>(smem);  // padded [n_top + 1]
+  unsigned char* stage = smem + a.pre_bytes + warp * a.stage_bytes;
+  uint32_t phase = 0u;
+  if (a.use_bulk && lane == 0) {
+    per_mbar_init(&s_mbar[warp], 1);
+    per_fence_mbar_init();
+  }
 
-  PerGridBarrier bar;
-  bar.init(t.scratch);
+  // early, independent loads: generation of the max exchange, size, first uniform
+  const uint32_t gen = lane == 0 ? per_ld_acquire(&sc->mx_gen) : 0u;
+  const int64_t size = __ldg(t.size_cursor);
+  int64_t tile = blockIdx.x;
+  float rnd0 = 0.f;
+  {
+    const int64_t j = tile * tile_draws + threadIdx.x;
+    if (tile < a.num_tiles && j < a.batch) rnd0 = __ldg(a.rand + j);
+  }
 
-  const int64_t size = t.size_cursor[0];
+  // ---- prologue: float64 exclusive prefix of the top level in shared memory
+  {
+    const float4* topv4 = reinterpret_cast<const float4*>(t.levels[top]);
+    const int nv4 = n_top >> 2;  // n_top is a multiple of 32
+    const int per = (nv4 + nthreads - 1) / nthreads;
+    const int beg = min(threadIdx.x * per, nv4);
+    const int end = min(beg + per, nv4);
+    constexpr int kReg = 8;  // float4 per thread kept in registers
+    float4 q[kReg];
+    double loc = 0.0;
+#pragma unroll
+    for (int i = 0; i < kReg; ++i)
+      q[i] = beg + i < end ? __ldg(topv4 + beg + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = beg + kReg; i0 < end; ++i0) {  // long segments (few threads, big top level)
+      const float4 v = __ldg(topv4 + i0);
+      loc += (double)v.x;
+      loc += (double)v.y;
+      loc += (double)v.z;
+      loc += (double)v.w;
+    }
+    double head = 0.0;
+#pragma unroll
+    for (int i = 0; i < kReg; ++i) {
+      head += (double)q[i].x;
+      head += (double)q[i].y;
+      head += (double)q[i].z;
+      head += (double)q[i].w;
+    }
+    loc += head;
+    const double incl = per_warp_scan_incl(loc, lane);
+    if (lane == 31) s_wsum[warp] = incl;
+    __syncthreads();
+    double run = incl - loc;
+    for (int k = 0; k < warp; ++k) run += s_wsum[k];
+#pragma unroll
+    for (int i = 0; i < kReg; ++i) {
+      if (beg + i < end) {
+        const int e = (beg + i) * 4;
+        s_pre[ppos(e)] = run;
+        run += (double)q[i].x;
+        s_pre[ppos(e + 1)] = run;
+        run += (double)q[i].y;
+        s_pre[ppos(e + 2)] = run;
+        run += (double)q[i].z;
+        s_pre[ppos(e + 3)] = run;
+        run += (double)q[i].w;
+      }
+    }
+    for (int i0 = beg + kReg; i0 < end; ++i0) {
+      const float4 v = __ldg(topv4 + i0);
+      const int e = i0 * 4;
+      s_pre[ppos(e)] = run;
+      run += (double)v.x;
+      s_pre[ppos(e + 1)] = run;
+      run += (double)v.y;
+      s_pre[ppos(e + 2)] = run;
+      run += (double)v.z;
+      s_pre[ppos(e + 3)] = run;
+      run += (double)v.w;
+    }
+    if (end == nv4 && end > beg) s_pre[ppos(n_top)] = run;
+    __syncthreads();
+  }
   if (size <= 0) {  // host checks first; keep the device consistent anyway
     if (blockIdx.x == 0 && threadIdx.x == 0) per_flag(t.status, PER_EVT_EMPTY_BUFFER);
     return;
   }
-
-  // ---- prologue: float64 exclusive prefix of the top level in shared memory
-  const int top = t.top_level;
-  const float* topv = t.levels[top];
-  const int n_top = (int)t.level_len[top];
-  {
-    const int per = (n_top + blockDim.x - 1) / blockDim.x;
-    const int beg = threadIdx.x * per;
-    double loc = 0.0;
-    for (int i = 0; i < per; ++i) {
-      const int q = beg + i;
-      if (q < n_top) loc += (double)__ldg(topv + q);
-    }
-    const double incl = per_warp_scan_incl(loc, lane);
-    if (lane == 31) s_wsum[warp] = incl;
-    if (threadIdx.x == 0) s_max_bits = 0u;
-    __syncthreads();
-    if (warp == 0) {
-      const double x = lane < nwarps ? s_wsum[lane] : 0.0;
-      const double xi = per_warp_scan_incl(x, lane);
-      __syncwarp();
-      s_wsum[lane] = xi - x;  // exclusive prefix of warp totals
-    }
-    __syncthreads();
-    double run = s_wsum[warp] + (incl - loc);
-    for (int i = 0; i < per; ++i) {
-      const int q = beg + i;
-      if (q < n_top) {
-        s_pre[q] = run;
-        run += (double)__ldg(topv + q);
-        if (q == n_top - 1) s_pre[n_top] = run;
-      }
-    }
-    __syncthreads();
-  }
-  const double total64 = s_pre[n_top];
+  const double total64 = s_pre[ppos(n_top)];
   const float total = __double2float_rn(total64);
   const float sizef = (float)size;
-
-  // ---- search: DPW draws per warp at a time
-  const int64_t s0 = (int64_t)blockIdx.x * a.draws_per_cta;
-  const int64_t e0 = min(s0 + a.draws_per_cta, a.batch);
-  uint32_t local_max = 0u;
-  uint32_t n_fallback = 0, n_clamp = 0, n_zero = 0;
   const float* leaves = t.levels[0];
+  uint32_t n_fallback = 0, n_clamp = 0, n_zero = 0;
+  uint32_t wmax_bits = 0u;
+  const uint32_t arrivals = gridDim.x * (uint32_t)(nthreads >> 5);
 
-  for (int64_t g = s0 + (int64_t)warp * kDPW; g < e0; g += (int64_t)nwarps * kDPW) {
-    int64_t node[kDPW];
-    double r[kDPW];
-    bool ok[kDPW], fb[kDPW];
-    float pv[kDPW];
-#pragma unroll
-    for (int d = 0; d < kDPW; ++d) {
-      const int64_t j = g + d;
-      ok[d] = j < e0;
-      fb[d] = false;
-      pv[d] = 0.f;
-      const float u = __fmul_rn(ok[d] ? __ldg(a.rand + j) : 0.f, total);
-      const double tu = (double)u;
-      int k = top_upper_bound(s_pre, n_top, tu, lane);
-      if (k >= n_top) {  // u >= total: fall back to the last node with mass
-        k = top_lower_bound(s_pre, n_top, total64, lane);
-        if (k >= n_top) k = n_top - 1;
-        fb[d] = true;
-      }
-      node[d] = k;
-      r[d] = tu - s_pre[k];
+  for (; tile < a.num_tiles; tile += gridDim.x) {
+    const bool last_tile = tile + gridDim.x >= a.num_tiles;
+    const int64_t wj0 = tile * tile_draws + warp * 32;  // first draw of this warp
+    const int64_t j = wj0 + lane;
+    const bool ok = j < a.batch;
+    const float rnd = tile == blockIdx.x ? rnd0 : (ok ? __ldg(a.rand + j) : 0.f);
+
+    // top level: binary search of the staged prefix
+    const float u = __fmul_rn(rnd, total);
+    double r = (double)u;
+    bool fb = false;
+    int k = upper_bound_pre(s_pre, n_top, r);
+    if (k >= n_top) {  // u at or past the total: last node with mass
+      k = lower_bound_pre(s_pre, n_top, total64);
+      if (k >= n_top) k = n_top - 1;
+      fb = true;
     }
+    int64_t node = k;
+    r -= s_pre[ppos(k)];
+    float p = 0.f;
+
+    // lower levels: stage each draw's 32 children, search them per lane
     for (int L = top - 1; L >= 0; --L) {
-      const float* lv = t.levels[L];
-      float v[kDPW];
+      __syncwarp();
+      per_stage_lines(t.levels[L], stage, 32, lane,
+                      [&](int d) { return __shfl_sync(PER_FULL_MASK, node, d); });
+      const float4* my = reinterpret_cast<const float4*>(stage + lane * PER_LINE_STRIDE);
+      float c[32];
 #pragma unroll
-      for (int d = 0; d < kDPW; ++d) v[d] = ok[d] ? __ldg(lv + node[d] * PER_FANOUT + lane) : 0.f;
-#pragma unroll
-      for (int d = 0; d < kDPW; ++d) {
-        const double sc = per_warp_scan_incl((double)v[d], lane);
-        const uint32_t m = __ballot_sync(PER_FULL_MASK, sc > r[d]);
-        int f;
-        if (m) {
-          f = __ffs(m) - 1;
-        } else {  // rounding: residual at or past this node's sum
-          const uint32_t mp = __ballot_sync(PER_FULL_MASK, v[d] > 0.f);
-          f = mp ? 31 - __clz(mp) : 0;
-          fb[d] = true;
-        }
-        double ex = __shfl_sync(PER_FULL_MASK, sc, f > 0 ? f - 1 : 0);
-        if (f == 0) ex = 0.0;
-        r[d] -= ex;
-        node[d] = node[d] * PER_FANOUT + f;
-        if (L == 0) pv[d] = __shfl_sync(PER_FULL_MASK, v[d], f);
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = my[i];
+        c[4 * i] = v.x;
+        c[4 * i + 1] = v.y;
+        c[4 * i + 2] = v.z;
+        c[4 * i + 3] = v.w;
       }
+      double ex;
+      const int f = search32(c, r, &ex, &p, &fb);
+      r -= ex;
+      node = node * PER_FANOUT + f;
     }
-#pragma unroll
-    for (int d = 0; d < kDPW; ++d) {
-      if (!ok[d]) continue;  // warp-uniform
-      int64_t i = node[d];
-      float p = pv[d];
+
+    int64_t i = node;
+    float wv = 0.f;
+    if (ok) {
       if (i > size - 1 || total64 <= 0.0) {  // sampling.py:49-51 clamp; p reloaded there
         i = size - 1;
         p = __ldg(leaves + i);
         ++n_clamp;
       }
       if (!(p > 0.f)) {  // never hand out an empty slot: walk back to the last positive one
-        int64_t c = i >> PER_LOG_FANOUT;
-        for (int it = 0; it < 64 && c >= 0; ++it, --c) {
-          const int64_t q = c * PER_FANOUT + lane;
-          const float vq = q <= i ? __ldg(leaves + q) : 0.f;
-          const uint32_t mp = __ballot_sync(PER_FULL_MASK, vq > 0.f);
-          if (mp) {
-            const int f = 31 - __clz(mp);
-            i = c * PER_FANOUT + f;
-            p = __shfl_sync(PER_FULL_MASK, vq, f);
+        int64_t cb = i >> PER_LOG_FANOUT;
+        for (int it = 0; it < 2048 && cb >= 0; ++it, --cb) {
+          int found = -1;
+          for (int q = 31; q >= 0; --q) {
+            const int64_t s = cb * PER_FANOUT + q;
+            if (s <= i && __ldg(leaves + s) > 0.f) {
+              found = q;
+              break;
+            }
+          }
+          if (found >= 0) {
+            i = cb * PER_FANOUT + found;
+            p = __ldg(leaves + i);
             break;
           }
         }
         ++n_zero;
       }
-      n_fallback += fb[d] ? 1u : 0u;
+      n_fallback += fb ? 1u : 0u;
       const float prob = __fdiv_rn(p, total);
-      const float wv = powf(__fmul_rn(sizef, prob), -a.beta);
-      local_max = max(local_max, __float_as_uint(wv));
-      if (lane == d) {
-        a.idx[g + d] = i;
-        a.w[g + d] = wv;
+      wv = powf(__fmul_rn(sizef, prob), -a.beta);
+      wmax_bits = max(wmax_bits, __float_as_uint(wv));
+    }
+    if (last_tile) {
+      // ---- arrive: publish this warp's max weight (before its stores, so the
+      // release below has nothing of this lane's to wait for)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        wmax_bits = max(wmax_bits, __shfl_xor_sync(PER_FULL_MASK, wmax_bits, o));
+      if (lane == 0) {
+        atomicMax(&sc->mx_bits[gen & 1u], wmax_bits);
+        const uint32_t old = per_atom_add_acq_rel(&sc->mx_count, 1u);
+        if (old == arrivals - 1) {  // last warp: reset for the next launch, release
+          sc->mx_count = 0u;
+          sc->mx_bits[(gen + 1u) & 1u] = 0u;
+          __threadfence();
+          per_st_release(&sc->mx_gen, gen + 1u);
+        }
       }
     }
+    if (ok) {
+      a.idx[j] = i;
+      a.w[j] = wv;
+    }
+    s_rows[warp][lane] = (int32_t)i;
+
+    // ---- gather this warp's rows
+    __syncwarp();
+    const int nrows = (int)min((int64_t)32, a.batch - wj0);
+    if (nrows > 0) {
+      if (a.use_bulk)
+        gather_bulk<VEC>(a, stage, s_rows[warp], wj0, nrows, lane, &s_mbar[warp], phase);
+      else if (a.rows_per_stage > 0)
+        gather_staged<VEC>(a, stage, s_rows[warp], wj0, nrows, lane);
+      else
+        gather_direct<VEC>(a, s_rows[warp], wj0, nrows, lane);
+    }
   }
+
   if (lane == 0) {
-    atomicMax(&s_max_bits, local_max);
     if (n_fallback) per_count(t.status, PER_STATUS_FALLBACKS, n_fallback);
     if (n_clamp) per_count(t.status, PER_STATUS_CLAMPS, n_clamp);
     if (n_zero) per_count(t.status, PER_STATUS_ZERO_WALKS, n_zero);
   }
-  __syncthreads();
-
-  // ---- arrive: publish this CTA's max weight
-  const bool multi = gridDim.x > 1;
-  if (multi) {
-    if (threadIdx.x == 0) {
-      t.scratch->partial[blockIdx.x] = __uint_as_float(s_max_bits);
-      s_last = bar.arrive_thread0() ? 1 : 0;
-    }
-    __syncthreads();
-    if (s_last) {  // last CTA: reduce the partial maxima and release the grid
-      __threadfence();
-      uint32_t m = 0u;
-      for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x)
-        m = max(m, __float_as_uint(__ldcg(&t.scratch->partial[i])));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(PER_FULL_MASK, m, o));
-      if (lane == 0) atomicMax(&s_max_bits, m);
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        t.scratch->gmax = __uint_as_float(s_max_bits);
-        bar.release_thread0();
+  // ---- wait until every warp has published, then normalise this warp's weights
+  uint32_t gbits = 0u;
+  if (lane == 0) {
+    uint32_t it = 0;
+    while (per_ld_acquire(&sc->mx_gen) == gen) {
+      if (++it > PER_SPIN_LIMIT) {
+        per_flag(t.status, PER_EVT_BARRIER_TIMEOUT);
+        per_count(t.status, PER_STATUS_TIMEOUTS);
+        break;
       }
+      __nanosleep(PER_SPIN_SLEEP_NS);
     }
+    gbits = per_ld_relaxed_u32(&sc->mx_bits[gen & 1u]);
   }
-
-  // ---- gather rows storage[idx[j]] -> out[j] (idx written above by this CTA)
-  {
-    using V = typename VecT<VEC>::T;
-    const int64_t nrows = e0 - s0;
-    const int64_t nitems = nrows * a.nseg;
-    const V* src_base = reinterpret_cast<const V*>(t.storage);
-    V* dst_base = reinterpret_cast<V*>(a.out);
-    const int64_t src_stride = t.row_stride / VEC;
-    const int64_t dst_stride = a.out_stride / VEC;
-    for (int64_t base = (int64_t)warp * kGatherUnroll; base < nitems;
-         base += (int64_t)nwarps * kGatherUnroll) {
-      V buf[kGatherUnroll][2];
-      const V* src[kGatherUnroll];
-      V* dst[kGatherUnroll];
-      int nv[kGatherUnroll];
-#pragma unroll
-      for (int u = 0; u < kGatherUnroll; ++u) {
-        const int64_t it = base + u;
-        nv[u] = 0;
-        if (it < nitems) {
-          const int64_t row = it / a.nseg;
-          const int sg = (int)(it - row * a.nseg);
-          const int64_t j = s0 + row;
-          const int64_t sidx = a.idx[j];
-          src[u] = src_base + sidx * src_stride + (int64_t)sg * kSegVec;
-          dst[u] = dst_base + j * dst_stride + (int64_t)sg * kSegVec;
-          nv[u] = min(kSegVec, a.nvec - sg * kSegVec);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kGatherUnroll; ++u) {
-        if (lane < nv[u]) buf[u][0] = __ldcs(src[u] + lane);
-        if (lane + 32 < nv[u]) buf[u][1] = __ldcs(src[u] + lane + 32);
-      }
-#pragma unroll
-      for (int u = 0; u < kGatherUnroll; ++u) {
-        if (lane < nv[u]) dst[u][lane] = buf[u][0];
-        if (lane + 32 < nv[u]) dst[u][lane + 32] = buf[u][1];
-      }
-    }
+  const float gmax = __uint_as_float(__shfl_sync(PER_FULL_MASK, gbits, 0));
+  for (int64_t tl = blockIdx.x; tl < a.num_tiles; tl += gridDim.x) {
+    const int64_t j = tl * tile_draws + warp * 32 + lane;
+    if (j < a.batch) a.w[j] = __fdiv_rn(a.w[j], gmax);
   }
-
-  // ---- wait for the global max, then normalise this CTA's weights
-  if (threadIdx.x == 0) {
-    if (multi) {
-      bar.wait_thread0(t.status);
-      s_gmax = per_ld_relaxed_f32(&t.scratch->gmax);
-    } else {
-      s_gmax = __uint_as_float(s_max_bits);
-    }
-  }
-  __syncthreads();
-  const float gmax = s_gmax;
-  for (int64_t j = s0 + threadIdx.x; j < e0; j += blockDim.x) a.w[j] = __fdiv_rn(a.w[j], gmax);
 }
 
 template <int VEC>
-int launch_vec(const SampleArgs& a0, cudaStream_t stream) {
-  SampleArgs a = a0;
+int launch_vec(SampleArgs a, cudaStream_t stream) {
   const void* fn = (const void*)per_sample_kernel<VEC>;
-  const size_t smem = (size_t)(a.t.level_len[a.t.top_level] + 1) * sizeof(double);
-  int max_ctas = 0;
-  int rc = per_coresident_ctas(fn, kSampleThreads, smem, &max_ctas);
+  // warps per CTA: spread small batches one warp per SM, up to 8 warps per CTA
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int64_t warp_tiles = (a.batch + 31) / 32;
+  int64_t nw = (warp_tiles + sms - 1) / sms;
+  if (nw < 1) nw = 1;
+  if (nw > kMaxWarps) nw = kMaxWarps;
+  // a few rows per SM: cp.async has the lower latency; many: bulk copies
+  // keep more rows in flight
+  if (a.use_bulk && warp_tiles <= sms && a.row_bytes <= kStageMax) {
+    a.use_bulk = 0;
+    a.row_bytes = (int32_t)(a.t.row_dim * 4);
+    a.rows_per_stage = (int32_t)(kStageMax / a.row_bytes < 32 ? kStageMax / a.row_bytes : 32);
+  }
+  const int threads = (int)nw * 32;
+  const int n_top = (int)a.t.level_len[a.t.top_level];
+  a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 15) & ~15;
+  const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
+  int rc = per_set_smem(fn, (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes);
   if (rc) return rc;
-  if (max_ctas > PER_MAX_GRID) max_ctas = PER_MAX_GRID;
-  const int64_t per_cta_min = (int64_t)(kSampleThreads / 32) * kDPW;
-  int64_t grid = (a.batch + per_cta_min - 1) / per_cta_min;
-  if (grid > max_ctas) grid = max_ctas;
+  int max_ctas = 0;
+  rc = per_coresident_ctas(fn, threads, smem, &max_ctas);
+  if (rc) return rc;
+  if ((int64_t)max_ctas * nw > PER_MAX_GRID * 8) max_ctas = (int)(PER_MAX_GRID * 8 / nw);
+  a.num_tiles = (a.batch + threads - 1) / threads;
+  int64_t grid = a.num_tiles < max_ctas ? a.num_tiles : max_ctas;
   if (grid < 1) grid = 1;
-  a.draws_per_cta = (a.batch + grid - 1) / grid;
-  grid = (a.batch + a.draws_per_cta - 1) / a.draws_per_cta;
   void* args[] = {&a};
-  cudaError_t e = per_launch(fn, (unsigned)grid, kSampleThreads, smem, stream, args, grid > 1);
+  cudaError_t e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, true);
   return e == cudaSuccess ? PER_OK : per_record_cuda(e);
 }
 
@@ -369,13 +579,32 @@ int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float 
   a.out_stride = out_stride;
   a.idx = idx;
   a.w = w;
-  a.draws_per_cta = 0;
+  a.num_tiles = 0;
+  a.pre_bytes = 0;
   // widest vector that every row start and both bases allow
-  const uintptr_t al = (uintptr_t)t.storage | (uintptr_t)out |
-                       (uintptr_t)(t.row_stride * 4) | (uintptr_t)(out_stride * 4);
-  const int vec = (al % 16 == 0 && t.row_dim % 4 == 0) ? 4 : (al % 8 == 0 && t.row_dim % 2 == 0) ? 2 : 1;
+  const uintptr_t al = (uintptr_t)t.storage | (uintptr_t)out | (uintptr_t)(t.row_stride * 4) |
+                       (uintptr_t)(out_stride * 4);
+  const int vec =
+      (al % 16 == 0 && t.row_dim % 4 == 0) ? 4 : (al % 8 == 0 && t.row_dim % 2 == 0) ? 2 : 1;
   a.nvec = (int32_t)(t.row_dim / vec);
-  a.nseg = (a.nvec + kSegVec - 1) / kSegVec;
+  // bulk copies need 16-byte aligned row starts; they copy row_dim*4 rounded
+  // up to 16 bytes, which must stay inside the row stride
+  const int64_t bulk_bytes = (t.row_dim * 4 + 15) / 16 * 16;
+  const bool bulk = ((uintptr_t)t.storage % 16 == 0) && ((t.row_stride * 4) % 16 == 0) &&
+                    bulk_bytes <= t.row_stride * 4 && bulk_bytes <= kStageMax;
+  const int64_t row_bytes = bulk ? bulk_bytes : t.row_dim * 4;
+  a.use_bulk = bulk ? 1 : 0;
+  a.row_bytes = (int32_t)row_bytes;
+  if (row_bytes <= kStageMax) {
+    const int64_t want = 32 * row_bytes;
+    a.stage_bytes = (int32_t)(want < kStageMax ? want : (kStageMax / row_bytes) * row_bytes);
+    a.rows_per_stage = (int32_t)(a.stage_bytes / row_bytes);
+  } else {
+    a.stage_bytes = 0;
+    a.rows_per_stage = 0;
+  }
+  if (a.stage_bytes < kStageMin) a.stage_bytes = kStageMin;  // the level tiles share it
+  a.stage_bytes = (a.stage_bytes + 15) & ~15;
   if (vec == 4) return launch_vec<4>(a, stream);
   if (vec == 2) return launch_vec<2>(a, stream);
   return launch_vec<1>(a, stream);

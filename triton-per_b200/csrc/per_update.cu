@@ -8,12 +8,18 @@
 //   buffer.py:66-79    add: ring write, new leaves = max priority, touched blocks recomputed
 //
 // Design: instead of fp32 delta atomics (which drift and need the periodic
-// refresh), every touched node is recomputed exactly from its 32 children in
-// float64, level by level, separated by grid barriers. Exactly one writer per
-// slot and per node is elected with atomicMax on a claim word, which makes the
-// result deterministic: for duplicate indices the last occurrence wins, and
-// the sums never drift. Claims are reset by their owner in the phase that
-// reads them, so the claim arrays are all-zero between launches.
+// refresh), every touched node is recomputed exactly from its 32 children
+// (one coalesced 128-byte warp load, float64 butterfly sum), level by level.
+// Exactly one writer per slot and per node is elected, which makes the result
+// deterministic: for duplicate indices the last occurrence wins, and the sums
+// never drift.
+//   * small batches (<= 1024 indices): one CTA, election in shared-memory
+//     hash tables, touched nodes listed per level and recomputed 32 per warp,
+//     levels separated by __syncthreads;
+//   * larger batches: a co-resident grid, election with atomicMax on global
+//     claim words, levels separated by grid barriers; claims are reset by
+//     their owner in the phase that reads them, so the claim arrays are
+//     all-zero between launches.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -36,14 +42,22 @@ struct UpdateArgs {
   int64_t n;
 };
 
+__device__ __forceinline__ float new_priority(const PerTree& t, float td) {
+  return powf(fabsf(td) + t.eps, t.alpha);  // update.py:32, buffer.py:139
+}
+
+// ---------------------------------------------------------------- grid update
 __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
   const PerTree& t = a.t;
   PerGridBarrier bar;
   bar.init(t.scratch);
   __shared__ uint32_t s_max;
+  __shared__ __align__(16) unsigned char s_tiles[kThreads / 32][PER_NODE_TILE];
   if (threadIdx.x == 0) s_max = 0u;
   __syncthreads();
 
+  const int lane = threadIdx.x & 31;
+  unsigned char* tile = s_tiles[threadIdx.x >> 5];
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t nth = (int64_t)gridDim.x * blockDim.x;
   uint32_t* tags = t.claims[0];
@@ -59,8 +73,7 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
       ++nbad;
       continue;
     }
-    const float np = powf(fabsf(a.td[e]) + t.eps, t.alpha);
-    tmax = max(tmax, __float_as_uint(np));
+    tmax = max(tmax, __float_as_uint(new_priority(t, a.td[e])));
     atomicMax(tags + i, (uint32_t)(e + 1));
     active |= 1u << q;
   }
@@ -70,7 +83,7 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
-  if ((threadIdx.x & 31) == 0 && tmax) atomicMax(&s_max, tmax);
+  if (lane == 0 && tmax) atomicMax(&s_max, tmax);
   __syncthreads();
   if (threadIdx.x == 0 && s_max) atomicMax(reinterpret_cast<unsigned int*>(t.max_priority), s_max);
 
@@ -84,27 +97,34 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
     const int64_t i = a.idx[e];
     if (__ldcg(tags + i) == (uint32_t)(e + 1)) {
       tags[i] = 0u;
-      leaves[i] = powf(fabsf(a.td[e]) + t.eps, t.alpha);
+      leaves[i] = new_priority(t, a.td[e]);
       atomicMax(t.claims[1] + (i >> PER_LOG_FANOUT), (uint32_t)(e + 1));
       next |= 1u << q;
     }
   }
   active = next;
 
-  // P2..: owners recompute their node from its 32 children, then claim the parent
+  // P2..: the owner of each touched node recomputes it (with its warp), then
+  // claims the parent
   for (int L = 1; L < t.num_levels; ++L) {
     bar.sync(t.status);
     next = 0u;
     uint32_t* cl = t.claims[L];
-    for (uint32_t m = active; m; m &= m - 1) {
+    const bool more = L + 1 < t.num_levels;
+    const uint32_t wmask = __reduce_or_sync(PER_FULL_MASK, active);
+    for (uint32_t m = wmask; m; m &= m - 1) {
       const int q = __ffs(m) - 1;
       const int64_t e = tid + (int64_t)q * nth;
-      const int64_t node = a.idx[e] >> (PER_LOG_FANOUT * L);
-      if (__ldcg(cl + node) == (uint32_t)(e + 1)) {
-        cl[node] = 0u;
-        t.levels[L][node] = __double2float_rn(per_sum32(t.levels[L - 1], node));
-        if (L + 1 < t.num_levels)
-          atomicMax(t.claims[L + 1] + (node >> PER_LOG_FANOUT), (uint32_t)(e + 1));
+      bool own = false;
+      int64_t node = 0;
+      if ((active >> q) & 1u) {
+        node = a.idx[e] >> (PER_LOG_FANOUT * L);
+        own = __ldcg(cl + node) == (uint32_t)(e + 1);
+        if (own) cl[node] = 0u;
+      }
+      per_warp_recompute(t.levels[L - 1], t.levels[L], node, own, lane, tile);
+      if (own) {
+        if (more) atomicMax(t.claims[L + 1] + (node >> PER_LOG_FANOUT), (uint32_t)(e + 1));
         next |= 1u << q;
       }
     }
@@ -112,6 +132,132 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- small update
+constexpr int kSmallMax = 1024;            // entries handled by the single CTA
+constexpr int kSmallPer = kSmallMax / kThreads;
+constexpr int kHashBits = 11;
+constexpr int kHash = 1 << kHashBits;      // >= 2 * kSmallMax: load factor <= 1/2
+constexpr uint32_t kEmpty = 0xffffffffu;
+constexpr size_t kSmallDynSmem = (size_t)(kThreads / 32) * PER_NODE_TILE;
+
+__device__ __forceinline__ uint32_t hslot(uint32_t key) {
+  return (key * 2654435761u) >> (32 - kHashBits);
+}
+
+// Insert key (set semantics); returns its slot, or -1 if the table is full.
+__device__ __forceinline__ int hset_insert(uint32_t* keys, uint32_t key) {
+  uint32_t s = hslot(key);
+  for (int probe = 0; probe < kHash; ++probe) {
+    const uint32_t prev = atomicCAS(&keys[s], kEmpty, key);
+    if (prev == kEmpty || prev == key) return (int)s;
+    s = (s + 1) & (kHash - 1);
+  }
+  return -1;
+}
+
+__global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a) {
+  const PerTree& t = a.t;
+  extern __shared__ __align__(16) unsigned char s_dyn[];  // per-warp node tiles
+  __shared__ uint32_t s_wkey[kHash];    // slot -> leaf index
+  __shared__ uint32_t s_wval[kHash];    // slot -> winning position + 1
+  __shared__ uint32_t s_set[2][kHash];  // touched nodes of the current / next level
+  __shared__ uint32_t s_list[kSmallMax];
+  __shared__ uint32_t s_count;
+  __shared__ uint32_t s_max;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  unsigned char* tile = s_dyn + warp * PER_NODE_TILE;
+
+  // issue the input loads before clearing the tables
+  int64_t li[kSmallPer];
+  float tdv[kSmallPer];
+#pragma unroll
+  for (int q = 0; q < kSmallPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    li[q] = e < a.n ? a.idx[e] : -1;
+    tdv[q] = e < a.n ? a.td[e] : 0.f;
+  }
+  for (int k = threadIdx.x; k < kHash; k += kThreads) {
+    s_wkey[k] = kEmpty;
+    s_wval[k] = 0u;
+    s_set[0][k] = kEmpty;
+    s_set[1][k] = kEmpty;
+  }
+  if (threadIdx.x == 0) {
+    s_max = 0u;
+    s_count = 0u;
+  }
+  __syncthreads();
+
+  // P0: new priorities, winner election (largest position wins), max priority
+  int slot[kSmallPer];
+  float np[kSmallPer];
+  uint32_t tmax = 0u, nbad = 0u;
+#pragma unroll
+  for (int q = 0; q < kSmallPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    slot[q] = -1;
+    np[q] = 0.f;
+    if (e < a.n) {
+      if (li[q] < 0 || li[q] >= t.capacity) {
+        ++nbad;
+      } else {
+        np[q] = new_priority(t, tdv[q]);
+        tmax = max(tmax, __float_as_uint(np[q]));
+        slot[q] = hset_insert(s_wkey, (uint32_t)li[q]);
+        if (slot[q] >= 0) atomicMax(&s_wval[slot[q]], (uint32_t)(e + 1));
+      }
+    }
+  }
+  if (nbad) {
+    per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
+    per_flag(t.status, PER_EVT_BAD_INDEX);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
+  if (lane == 0 && tmax) atomicMax(&s_max, tmax);
+  __syncthreads();
+  if (threadIdx.x == 0 && s_max) atomicMax(reinterpret_cast<unsigned int*>(t.max_priority), s_max);
+
+  // P1: winners write their leaf; collect touched chunks
+#pragma unroll
+  for (int q = 0; q < kSmallPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    if (slot[q] >= 0 && s_wval[slot[q]] == (uint32_t)(e + 1)) {
+      t.levels[0][li[q]] = np[q];
+      hset_insert(s_set[0], (uint32_t)(li[q] >> PER_LOG_FANOUT));
+    }
+  }
+  __syncthreads();
+
+  // P2..: list the touched nodes, recompute them 32 per warp, collect parents
+  int cur = 0;
+  for (int L = 1; L < t.num_levels; ++L) {
+    uint32_t* set = s_set[cur];
+    uint32_t* nxt = s_set[cur ^ 1];
+    const bool more = L + 1 < t.num_levels;
+    for (int k = threadIdx.x; k < kHash; k += kThreads) {
+      const uint32_t node = set[k];
+      if (node != kEmpty) s_list[atomicAdd(&s_count, 1u)] = node;
+      set[k] = kEmpty;
+    }
+    __syncthreads();
+    const int cnt = (int)s_count;
+    for (int base = warp * 32; base < cnt; base += kThreads) {
+      const int k = base + lane;
+      const bool own = k < cnt;
+      const int64_t node = own ? (int64_t)s_list[k] : 0;
+      per_warp_recompute(t.levels[L - 1], t.levels[L], node, own, lane, tile);
+      if (own && more) hset_insert(nxt, (uint32_t)(node >> PER_LOG_FANOUT));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_count = 0u;
+    __syncthreads();
+    cur ^= 1;
+  }
+}
+
+// ---------------------------------------------------------------- add
 struct AddArgs {
   PerTree t;
   per_field_t fields[PER_MAX_FIELDS];
@@ -121,8 +267,11 @@ struct AddArgs {
 
 __global__ void __launch_bounds__(kThreads) per_add_kernel(AddArgs a) {
   const PerTree& t = a.t;
+  __shared__ __align__(16) unsigned char s_tiles[kThreads / 32][PER_NODE_TILE];
   PerGridBarrier bar;
   bar.init(t.scratch);
+  const int lane = threadIdx.x & 31;
+  unsigned char* tile = s_tiles[threadIdx.x >> 5];
   const int64_t C = t.capacity;
   const int64_t size = t.size_cursor[0];
   const int64_t cursor = t.size_cursor[1];
@@ -130,41 +279,39 @@ __global__ void __launch_bounds__(kThreads) per_add_kernel(AddArgs a) {
   const int64_t n0 = a.n > C ? a.n - C : 0;  // earlier rows would be overwritten in this call
   const int64_t m = a.n - n0;
   const int64_t start = (cursor + n0) % C;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
 
   // P0: rows and leaves (one warp per row)
-  {
-    const int lane = threadIdx.x & 31;
-    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t k = gw; k < m; k += nw) {
-      const int64_t src_row = n0 + k;
-      int64_t pos = start + k;
-      if (pos >= C) pos -= C;
-      float* dst = t.storage + pos * t.row_stride;
-      for (int f = 0; f < a.n_fields; ++f) {
-        const per_field_t& fd = a.fields[f];
-        const float* src = fd.data + src_row * fd.stride;
-        for (int64_t c = lane; c < fd.dim; c += 32) dst[fd.col_offset + c] = src[c];
-      }
-      if (lane == 0) t.levels[0][pos] = maxp;
+  for (int64_t k = gw; k < m; k += nw) {
+    const int64_t src_row = n0 + k;
+    int64_t pos = start + k;
+    if (pos >= C) pos -= C;
+    float* dst = t.storage + pos * t.row_stride;
+    for (int f = 0; f < a.n_fields; ++f) {
+      const per_field_t& fd = a.fields[f];
+      const float* src = fd.data + src_row * fd.stride;
+      for (int64_t c = lane; c < fd.dim; c += 32) dst[fd.col_offset + c] = src[c];
     }
+    if (lane == 0) t.levels[0][pos] = maxp;
   }
 
   // touched leaf ranges: [start, start+m) on the ring, split at C
   const int64_t a0 = start, a1 = min(start + m, C);
-  const int64_t b0 = 0, b1 = start + m > C ? start + m - C : 0;
-  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  const int64_t b1 = start + m > C ? start + m - C : 0;
   for (int L = 1; L < t.num_levels; ++L) {
     bar.sync(t.status);
     const int sh = PER_LOG_FANOUT * L;
     const int64_t lo0 = a0 >> sh, hi0 = (a1 - 1) >> sh;
     const int64_t cnt0 = a1 > a0 ? hi0 - lo0 + 1 : 0;
-    const int64_t lo1 = b0 >> sh, hi1 = b1 > b0 ? (b1 - 1) >> sh : -1;
-    const int64_t cnt1 = b1 > b0 ? hi1 - lo1 + 1 : 0;
-    for (int64_t k = tid; k < cnt0 + cnt1; k += nth) {
-      const int64_t node = k < cnt0 ? lo0 + k : lo1 + (k - cnt0);
-      t.levels[L][node] = __double2float_rn(per_sum32(t.levels[L - 1], node));
+    const int64_t hi1 = b1 > 0 ? (b1 - 1) >> sh : -1;
+    const int64_t cnt1 = b1 > 0 ? hi1 + 1 : 0;
+    const int64_t total = cnt0 + cnt1;
+    for (int64_t base = gw * 32; base < total; base += nw * 32) {
+      const int64_t k = base + lane;
+      const bool own = k < total;
+      const int64_t node = !own ? 0 : (k < cnt0 ? lo0 + k : k - cnt0);
+      per_warp_recompute(t.levels[L - 1], t.levels[L], node, own, lane, tile);
     }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -173,18 +320,27 @@ __global__ void __launch_bounds__(kThreads) per_add_kernel(AddArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- rebuild
 __global__ void __launch_bounds__(kThreads) per_rebuild_kernel(PerTree t) {
+  __shared__ __align__(16) unsigned char s_tiles[kThreads / 32][PER_NODE_TILE];
   PerGridBarrier bar;
   bar.init(t.scratch);
+  const int lane = threadIdx.x & 31;
+  unsigned char* tile = s_tiles[threadIdx.x >> 5];
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  const int64_t gw = tid >> 5;
+  const int64_t nw = nth >> 5;
   for (int L = 0; L < t.num_levels; ++L)
     for (int64_t k = tid; k < t.level_len[L]; k += nth) t.claims[L][k] = 0u;
   for (int L = 1; L < t.num_levels; ++L) {
     bar.sync(t.status);
     const int64_t nodes = live_nodes(t.capacity, L);
-    for (int64_t k = tid; k < nodes; k += nth)
-      t.levels[L][k] = __double2float_rn(per_sum32(t.levels[L - 1], k));
+    for (int64_t base = gw * 32; base < nodes; base += nw * 32) {
+      const int64_t node = base + lane;
+      per_warp_recompute(t.levels[L - 1], t.levels[L], node < nodes ? node : 0, node < nodes, lane,
+                         tile);
+    }
   }
 }
 
@@ -209,6 +365,14 @@ int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int
   a.idx = idx;
   a.td = td;
   a.n = n;
+  if (n <= kSmallMax) {
+    const void* fs = (const void*)per_update_small_kernel;
+    int rc = per_set_smem(fs, kSmallDynSmem);
+    if (rc) return rc;
+    void* args[] = {&a};
+    cudaError_t e = per_launch(fs, 1, kThreads, kSmallDynSmem, stream, args, false);
+    return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+  }
   const void* fn = (const void*)per_update_kernel;
   int grid = 0;
   int rc = grid_for(fn, n, &grid);

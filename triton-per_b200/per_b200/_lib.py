@@ -84,6 +84,7 @@ class Field(ctypes.Structure):
 # name -> (restype, argtypes); every function declared in include/per_b200.h
 SIGNATURES = {
     "per_layout": (ctypes.c_int, [i64, ctypes.POINTER(Layout)]),
+    "per_row_stride": (i64, [i64]),
     "per_sample_fused": (ctypes.c_int, [ctypes.POINTER(Store), vp, i64, ctypes.c_float, vp, i64,
                                         vp, vp, vp]),
     "per_update_priorities": (ctypes.c_int, [ctypes.POINTER(Store), vp, vp, i64, vp]),
@@ -99,7 +100,7 @@ def header_functions(path: str = HEADER) -> list[str]:
     """Names of the functions that include/per_b200.h declares."""
     text = open(path).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return re.findall(r"^\s*(?:int|const char\*|void)\s+(per_\w+)\s*\(", text, flags=re.M)
+    return re.findall(r"^\s*(?:int|int64_t|const char\*|void)\s+(per_\w+)\s*\(", text, flags=re.M)
 
 
 def _load():

@@ -5,9 +5,10 @@ Drop-in for triton-per's `PERBuffer` with its `triton` backend
 `sample(batch_size, beta) -> (views, idx, w)` and
 `update_priorities(indices, td_errors)`, and the module constant BLOCK_P.
 
-Storage is one packed float32[capacity, row_dim] tensor and sampling returns
-zero-copy field views of a freshly allocated [batch, row_dim] output, as in the
-reference. Priorities live in the reference's two-level store (leaves padded
+Storage is one float32[capacity, row_dim] view (rows padded in memory to a
+16-byte multiple stride, see per_row_stride, so that rows can be gathered with
+bulk copies) and sampling returns zero-copy field views of a freshly allocated
+packed [batch, row_dim] output, as in the reference. Priorities live in the reference's two-level store (leaves padded
 to BLOCK_P per block plus float32 block sums), widened into a 32-ary sum tree:
 the engine also keeps 32-leaf chunk sums (and, above 4M slots, sums of 32
 blocks) so that every level of a search is one coalesced warp load.
@@ -75,7 +76,9 @@ class PERBuffer:
         self.top_level = int(lay.top_level)
 
         dev = self.device
-        self.storage = torch.zeros(capacity, self.row_dim, device=dev)
+        self.row_stride = int(_lib.lib.per_row_stride(self.row_dim))
+        self._storage = torch.zeros(capacity, self.row_stride, device=dev)
+        self.storage = self._storage[:, : self.row_dim]
         self._levels = [torch.zeros(int(lay.level_len[k]), device=dev)
                         for k in range(self.num_levels)]
         self.priorities = self._levels[0]
@@ -99,9 +102,9 @@ class PERBuffer:
         s.num_levels = self.num_levels
         s.top_level = self.top_level
         s.capacity = capacity
-        s.storage = self.storage.data_ptr()
+        s.storage = self._storage.data_ptr()
         s.row_dim = self.row_dim
-        s.row_stride = self.row_dim
+        s.row_stride = self.row_stride
         s.size_cursor = self._size_cursor.data_ptr()
         s.max_priority = self._max_priority.data_ptr()
         s.status = self._status.data_ptr()
