@@ -129,6 +129,10 @@ int per_set_smem(const void* fn, size_t smem) {
     if (done[i].device == dev && done[i].fn == fn && done[i].smem >= smem) return PER_OK;
   e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return per_record_cuda(e);
+  // prefer the largest shared-memory carveout, so that several CTAs fit per SM
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return per_record_cuda(e);
   for (int i = 0; i < n_done; ++i)
     if (done[i].device == dev && done[i].fn == fn) {
       done[i].smem = smem;

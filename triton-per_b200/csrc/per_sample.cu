@@ -59,6 +59,7 @@ struct SampleArgs {
   int32_t stage_bytes;     // per-warp staging bytes
   int32_t row_bytes;       // staged bytes per row (bulk: row_dim*4 rounded up to 16)
   int32_t use_bulk;        // rows are 16-byte aligned: gather with bulk copies
+  int32_t cp_bytes;        // cp.async piece size when not using bulk copies (4, 8, 16)
   int32_t pre_bytes;       // bytes of the padded prefix array
   int64_t num_tiles;
 };
@@ -173,8 +174,9 @@ __device__ __forceinline__ void cp_async(uint32_t saddr, const void* g, int byte
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(saddr), "l"(g) : "memory");
 }
 
-// Store staged rows (row r at r * spitch vectors) to out rows j0 + r, as one
-// flat lane-strided walk over all vectors (coalesced stores).
+// Store staged rows (row r at r * spitch vectors) to out rows j0 + r.
+// Rows of >= 32 vectors: one flat lane-strided walk (coalesced stores);
+// shorter rows: each lane stores its own row.
 template <int VEC>
 __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stage, int spitch,
                                            int64_t j0, int rn, int lane) {
@@ -183,13 +185,9 @@ __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stag
   const V* sv = reinterpret_cast<const V*>(stage);
   V* dst = reinterpret_cast<V*>(a.out) + j0 * (a.out_stride / VEC);
   const int dstride = (int)(a.out_stride / VEC);
-  const int pieces = rn * nvec;
   if (nvec >= 32) {  // at most one row wrap per step of 32
+    const int pieces = rn * nvec;
     int r = 0, c = lane;
-    if (c >= nvec) {
-      c -= nvec;
-      ++r;
-    }
     for (int p = lane; p < pieces; p += 32) {
       dst[r * dstride + c] = sv[r * spitch + c];
       c += 32;
@@ -198,59 +196,48 @@ __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stag
         ++r;
       }
     }
-  } else {
-    for (int p = lane; p < pieces; p += 32) {
-      const int r = p / nvec, c = p - r * nvec;
-      dst[r * dstride + c] = sv[r * spitch + c];
-    }
+  } else if (lane < rn) {
+    for (int c = 0; c < nvec; ++c) dst[lane * dstride + c] = sv[lane * spitch + c];
   }
 }
 
-// Rows through shared memory with cp.async: lowest latency for a few rows
-// per SM (rows at any 4-byte alignment).
-template <int VEC>
-__device__ __forceinline__ void gather_staged(const SampleArgs& a, unsigned char* stage,
-                                              const int32_t* s_idx, int64_t j0, int nrows,
-                                              int lane) {
-  using V = typename VecT<VEC>::T;
-  const int nvec = a.nvec;
-  const uint32_t sbase = per_smem_addr(stage);
-  const V* src = reinterpret_cast<const V*>(a.t.storage);
-  const int64_t sstride = a.t.row_stride / VEC;
-  for (int r0 = 0; r0 < nrows; r0 += a.rows_per_stage) {
-    const int rn = min(a.rows_per_stage, nrows - r0);
-    const int pieces = rn * nvec;
-    for (int p = lane; p < pieces; p += 32) {
-      const int r = p / nvec, c = p - r * nvec;
-      cp_async(sbase + (uint32_t)(p * VEC * 4), src + (int64_t)s_idx[r0 + r] * sstride + c, VEC * 4);
-    }
-    per_cp_async_wait_all();
-    __syncwarp();
-    store_rows<VEC>(a, stage, nvec, j0 + r0, rn, lane);
-    __syncwarp();
-  }
-}
-
-// Rows through shared memory with one bulk copy per lane (16-byte aligned rows).
-template <int VEC>
-__device__ __forceinline__ void gather_bulk(const SampleArgs& a, unsigned char* stage,
-                                            const int32_t* s_idx, int64_t j0, int nrows,
-                                            int lane, uint64_t* mbar, uint32_t& phase) {
-  const float* src = a.t.storage;
-  for (int r0 = 0; r0 < nrows; r0 += a.rows_per_stage) {
-    const int rn = min(a.rows_per_stage, nrows - r0);
+// Issue the copies of rows s_idx[r0 .. r0+rn) into the warp's tile: one
+// Tensor Memory Accelerator bulk copy per lane (16-byte aligned rows), or
+// one cp.async chain per lane (any 4-byte alignment; lower latency when an SM
+// has only a few rows to fetch).
+__device__ __forceinline__ void gather_issue(const SampleArgs& a, unsigned char* stage,
+                                             const int32_t* s_idx, int r0, int rn, int lane,
+                                             uint64_t* mbar) {
+  const float* row = a.t.storage + (int64_t)s_idx[r0 + min(lane, rn - 1)] * a.t.row_stride;
+  if (a.use_bulk) {
     per_fence_proxy_async_smem();  // earlier generic accesses of the tile before the bulk writes
     __syncwarp();
     if (lane == 0) per_mbar_arrive_expect_tx(mbar, (uint32_t)(rn * a.row_bytes));
     __syncwarp();
-    if (lane < rn)
-      per_bulk_load(stage + lane * a.row_bytes, src + (int64_t)s_idx[r0 + lane] * a.t.row_stride,
-                    (uint32_t)a.row_bytes, mbar);
+    if (lane < rn) per_bulk_load(stage + lane * a.row_bytes, row, (uint32_t)a.row_bytes, mbar);
+  } else if (lane < rn) {
+    const uint32_t dst = per_smem_addr(stage + lane * a.row_bytes);
+    const int cpb = a.cp_bytes;
+    const int pieces = a.row_bytes / cpb;
+    const char* src = reinterpret_cast<const char*>(row);
+    for (int k = 0; k < pieces; ++k) cp_async(dst + (uint32_t)(k * cpb), src + k * cpb, cpb);
+  }
+}
+
+// Wait for the copies issued by gather_issue and store the rows out.
+template <int VEC>
+__device__ __forceinline__ void gather_finish(const SampleArgs& a, unsigned char* stage,
+                                              int64_t j0, int rn, int lane, uint64_t* mbar,
+                                              uint32_t& phase) {
+  if (a.use_bulk) {
     per_mbar_wait(mbar, phase, a.t.status);
     phase ^= 1u;
-    store_rows<VEC>(a, stage, a.row_bytes / (VEC * 4), j0 + r0, rn, lane);
-    __syncwarp();
+  } else {
+    per_cp_async_wait_all();
   }
+  __syncwarp();
+  store_rows<VEC>(a, stage, a.row_bytes / (VEC * 4), j0, rn, lane);
+  __syncwarp();
 }
 
 // Wide rows: each row copied directly by the whole warp, 8 vectors per lane in flight.
@@ -283,40 +270,56 @@ __device__ __forceinline__ void gather_direct(const SampleArgs& a, const int32_t
   }
 }
 
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Named barriers between the compute warps and the CTA's helper warp.
+constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
+constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
+
 template <int VEC>
-__global__ void __launch_bounds__(kMaxWarps * 32) per_sample_kernel(SampleArgs a) {
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(SampleArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ double s_wsum[kMaxWarps];
+  __shared__ double s_wsum[kMaxWarps + 1];
   __shared__ int32_t s_rows[kMaxWarps][32];
   __shared__ uint64_t s_mbar[kMaxWarps];
+  __shared__ uint32_t s_cta_max;
+  __shared__ float s_gmax;
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nthreads = blockDim.x;
-  const int64_t tile_draws = nthreads;
+  const int nwarps = (nthreads >> 5) - 1;  // compute warps; the last warp is the helper
+  const bool helper = warp == nwarps;
+  const int64_t tile_draws = (int64_t)nwarps * 32;
   const PerTree& t = a.t;
   PerScratch* sc = t.scratch;
   const int top = t.top_level;
   const int n_top = (int)t.level_len[top];
   double* s_pre = reinterpret_cast<double*>(smem);  // padded [n_top + 1]
-  unsigned char* stage = smem + a.pre_bytes + warp * a.stage_bytes;
+  unsigned char* stage = smem + a.pre_bytes + (helper ? 0 : warp) * a.stage_bytes;
   uint32_t phase = 0u;
-  if (a.use_bulk && lane == 0) {
+  if (!helper && a.use_bulk && lane == 0) {
     per_mbar_init(&s_mbar[warp], 1);
     per_fence_mbar_init();
   }
 
   // early, independent loads: generation of the max exchange, size, first uniform
-  const uint32_t gen = lane == 0 ? per_ld_acquire(&sc->mx_gen) : 0u;
+  const uint32_t gen = helper && lane == 0 ? per_ld_relaxed_u32(&sc->mx_gen) : 0u;
   const int64_t size = __ldg(t.size_cursor);
   int64_t tile = blockIdx.x;
   float rnd0 = 0.f;
-  {
+  if (!helper) {
     const int64_t j = tile * tile_draws + threadIdx.x;
     if (tile < a.num_tiles && j < a.batch) rnd0 = __ldg(a.rand + j);
   }
 
-  // ---- prologue: float64 exclusive prefix of the top level in shared memory
+  // ---- prologue (all warps): float64 exclusive prefix of the top level
   {
     const float4* topv4 = reinterpret_cast<const float4*>(t.levels[top]);
     const int nv4 = n_top >> 2;  // n_top is a multiple of 32
@@ -347,6 +350,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) per_sample_kernel(SampleArgs a
     loc += head;
     const double incl = per_warp_scan_incl(loc, lane);
     if (lane == 31) s_wsum[warp] = incl;
+    if (threadIdx.x == 0) s_cta_max = 0u;
     __syncthreads();
     double run = incl - loc;
     for (int k = 0; k < warp; ++k) run += s_wsum[k];
@@ -383,13 +387,44 @@ __global__ void __launch_bounds__(kMaxWarps * 32) per_sample_kernel(SampleArgs a
     if (blockIdx.x == 0 && threadIdx.x == 0) per_flag(t.status, PER_EVT_EMPTY_BUFFER);
     return;
   }
+
+  if (helper) {
+    // ---- helper warp: exchange the batch max with the other CTAs while the
+    // compute warps gather their rows
+    named_bar_sync(kBarMaxReady, nthreads);
+    if (lane == 0) {
+      atomicMax(&sc->mx_bits[gen & 1u], s_cta_max);
+      const uint32_t old = per_atom_add_acq_rel(&sc->mx_count, 1u);
+      if (old == gridDim.x - 1) {  // last CTA: reset for the next launch, then release
+        sc->mx_count = 0u;
+        sc->mx_bits[(gen + 1u) & 1u] = 0u;
+        __threadfence();
+        per_st_release(&sc->mx_gen, gen + 1u);
+      }
+      uint32_t it = 0;
+      while (per_ld_acquire(&sc->mx_gen) == gen) {
+        if (++it > PER_SPIN_LIMIT) {
+          per_flag(t.status, PER_EVT_BARRIER_TIMEOUT);
+          per_count(t.status, PER_STATUS_TIMEOUTS);
+          break;
+        }
+        __nanosleep(PER_SPIN_SLEEP_NS);
+      }
+      s_gmax = __uint_as_float(per_ld_relaxed_u32(&sc->mx_bits[gen & 1u]));
+    }
+    __syncwarp();
+    named_bar_arrive(kBarGmaxReady, nthreads);
+    return;
+  }
+
+  // ---- compute warps
   const double total64 = s_pre[ppos(n_top)];
   const float total = __double2float_rn(total64);
   const float sizef = (float)size;
   const float* leaves = t.levels[0];
   uint32_t n_fallback = 0, n_clamp = 0, n_zero = 0;
   uint32_t wmax_bits = 0u;
-  const uint32_t arrivals = gridDim.x * (uint32_t)(nthreads >> 5);
+  float w_last = 0.f;  // this lane's unnormalised weight in its last tile
 
   for (; tile < a.num_tiles; tile += gridDim.x) {
     const bool last_tile = tile + gridDim.x >= a.num_tiles;
@@ -465,39 +500,32 @@ __global__ void __launch_bounds__(kMaxWarps * 32) per_sample_kernel(SampleArgs a
       wv = powf(__fmul_rn(sizef, prob), -a.beta);
       wmax_bits = max(wmax_bits, __float_as_uint(wv));
     }
-    if (last_tile) {
-      // ---- arrive: publish this warp's max weight (before its stores, so the
-      // release below has nothing of this lane's to wait for)
+    if (last_tile) {  // hand this warp's max to the helper warp and move on
+      w_last = wv;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1)
         wmax_bits = max(wmax_bits, __shfl_xor_sync(PER_FULL_MASK, wmax_bits, o));
-      if (lane == 0) {
-        atomicMax(&sc->mx_bits[gen & 1u], wmax_bits);
-        const uint32_t old = per_atom_add_acq_rel(&sc->mx_count, 1u);
-        if (old == arrivals - 1) {  // last warp: reset for the next launch, release
-          sc->mx_count = 0u;
-          sc->mx_bits[(gen + 1u) & 1u] = 0u;
-          __threadfence();
-          per_st_release(&sc->mx_gen, gen + 1u);
-        }
-      }
+      if (lane == 0) atomicMax(&s_cta_max, wmax_bits);
+      __syncwarp();
+      named_bar_arrive(kBarMaxReady, nthreads);
     }
     if (ok) {
       a.idx[j] = i;
-      a.w[j] = wv;
+      if (!last_tile) a.w[j] = wv;
     }
     s_rows[warp][lane] = (int32_t)i;
+    __syncwarp();
 
     // ---- gather this warp's rows
-    __syncwarp();
     const int nrows = (int)min((int64_t)32, a.batch - wj0);
-    if (nrows > 0) {
-      if (a.use_bulk)
-        gather_bulk<VEC>(a, stage, s_rows[warp], wj0, nrows, lane, &s_mbar[warp], phase);
-      else if (a.rows_per_stage > 0)
-        gather_staged<VEC>(a, stage, s_rows[warp], wj0, nrows, lane);
-      else
-        gather_direct<VEC>(a, s_rows[warp], wj0, nrows, lane);
+    if (a.rows_per_stage > 0) {
+      for (int r0 = 0; r0 < nrows; r0 += a.rows_per_stage) {
+        const int rn = min(a.rows_per_stage, nrows - r0);
+        gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp]);
+        gather_finish<VEC>(a, stage, wj0 + r0, rn, lane, &s_mbar[warp], phase);
+      }
+    } else if (nrows > 0) {
+      gather_direct<VEC>(a, s_rows[warp], wj0, nrows, lane);
     }
   }
 
@@ -506,31 +534,20 @@ __global__ void __launch_bounds__(kMaxWarps * 32) per_sample_kernel(SampleArgs a
     if (n_clamp) per_count(t.status, PER_STATUS_CLAMPS, n_clamp);
     if (n_zero) per_count(t.status, PER_STATUS_ZERO_WALKS, n_zero);
   }
-  // ---- wait until every warp has published, then normalise this warp's weights
-  uint32_t gbits = 0u;
-  if (lane == 0) {
-    uint32_t it = 0;
-    while (per_ld_acquire(&sc->mx_gen) == gen) {
-      if (++it > PER_SPIN_LIMIT) {
-        per_flag(t.status, PER_EVT_BARRIER_TIMEOUT);
-        per_count(t.status, PER_STATUS_TIMEOUTS);
-        break;
-      }
-      __nanosleep(PER_SPIN_SLEEP_NS);
-    }
-    gbits = per_ld_relaxed_u32(&sc->mx_bits[gen & 1u]);
-  }
-  const float gmax = __uint_as_float(__shfl_sync(PER_FULL_MASK, gbits, 0));
+  // ---- normalise this warp's weights by the global max from the helper warp
+  named_bar_sync(kBarGmaxReady, nthreads);
+  const float gmax = s_gmax;
   for (int64_t tl = blockIdx.x; tl < a.num_tiles; tl += gridDim.x) {
     const int64_t j = tl * tile_draws + warp * 32 + lane;
-    if (j < a.batch) a.w[j] = __fdiv_rn(a.w[j], gmax);
+    const bool last = tl + gridDim.x >= a.num_tiles;
+    if (j < a.batch) a.w[j] = __fdiv_rn(last ? w_last : a.w[j], gmax);
   }
 }
 
 template <int VEC>
 int launch_vec(SampleArgs a, cudaStream_t stream) {
   const void* fn = (const void*)per_sample_kernel<VEC>;
-  // warps per CTA: spread small batches one warp per SM, up to 8 warps per CTA
+  // compute warps per CTA: spread small batches one warp per SM, up to 8
   int sms = 148;
   {
     int dev = 0;
@@ -543,12 +560,8 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
   if (nw > kMaxWarps) nw = kMaxWarps;
   // a few rows per SM: cp.async has the lower latency; many: bulk copies
   // keep more rows in flight
-  if (a.use_bulk && warp_tiles <= sms && a.row_bytes <= kStageMax) {
-    a.use_bulk = 0;
-    a.row_bytes = (int32_t)(a.t.row_dim * 4);
-    a.rows_per_stage = (int32_t)(kStageMax / a.row_bytes < 32 ? kStageMax / a.row_bytes : 32);
-  }
-  const int threads = (int)nw * 32;
+  if (a.use_bulk && warp_tiles <= sms) a.use_bulk = 0;
+  const int threads = (int)(nw + 1) * 32;
   const int n_top = (int)a.t.level_len[a.t.top_level];
   a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 15) & ~15;
   const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
@@ -557,12 +570,11 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
   int max_ctas = 0;
   rc = per_coresident_ctas(fn, threads, smem, &max_ctas);
   if (rc) return rc;
-  if ((int64_t)max_ctas * nw > PER_MAX_GRID * 8) max_ctas = (int)(PER_MAX_GRID * 8 / nw);
-  a.num_tiles = (a.batch + threads - 1) / threads;
+  a.num_tiles = (a.batch + nw * 32 - 1) / (nw * 32);
   int64_t grid = a.num_tiles < max_ctas ? a.num_tiles : max_ctas;
   if (grid < 1) grid = 1;
   void* args[] = {&a};
-  cudaError_t e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, true);
+  cudaError_t e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, grid > 1);
   return e == cudaSuccess ? PER_OK : per_record_cuda(e);
 }
 
@@ -587,13 +599,19 @@ int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float 
   const int vec =
       (al % 16 == 0 && t.row_dim % 4 == 0) ? 4 : (al % 8 == 0 && t.row_dim % 2 == 0) ? 2 : 1;
   a.nvec = (int32_t)(t.row_dim / vec);
-  // bulk copies need 16-byte aligned row starts; they copy row_dim*4 rounded
-  // up to 16 bytes, which must stay inside the row stride
-  const int64_t bulk_bytes = (t.row_dim * 4 + 15) / 16 * 16;
-  const bool bulk = ((uintptr_t)t.storage % 16 == 0) && ((t.row_stride * 4) % 16 == 0) &&
-                    bulk_bytes <= t.row_stride * 4 && bulk_bytes <= kStageMax;
-  const int64_t row_bytes = bulk ? bulk_bytes : t.row_dim * 4;
-  a.use_bulk = bulk ? 1 : 0;
+  // staged copies move whole pieces: 16 bytes when row starts and strides are
+  // 16-byte aligned (rounding row_dim*4 up to 16 must stay inside the row
+  // stride), else 8, else 4; bulk copies need the 16-byte case
+  const int64_t rb = t.row_dim * 4;
+  const uintptr_t sal = (uintptr_t)t.storage | (uintptr_t)(t.row_stride * 4);
+  int cpb = 4;
+  if (sal % 16 == 0 && (rb + 15) / 16 * 16 <= t.row_stride * 4)
+    cpb = 16;
+  else if (sal % 8 == 0 && (rb + 7) / 8 * 8 <= t.row_stride * 4)
+    cpb = 8;
+  const int64_t row_bytes = (rb + cpb - 1) / cpb * cpb;
+  a.cp_bytes = cpb;
+  a.use_bulk = (cpb == 16) ? 1 : 0;
   a.row_bytes = (int32_t)row_bytes;
   if (row_bytes <= kStageMax) {
     const int64_t want = 32 * row_bytes;
@@ -602,6 +620,7 @@ int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float 
   } else {
     a.stage_bytes = 0;
     a.rows_per_stage = 0;
+    a.use_bulk = 0;
   }
   if (a.stage_bytes < kStageMin) a.stage_bytes = kStageMin;  // the level tiles share it
   a.stage_bytes = (a.stage_bytes + 15) & ~15;

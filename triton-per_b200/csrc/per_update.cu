@@ -14,8 +14,8 @@
 // deterministic: for duplicate indices the last occurrence wins, and the sums
 // never drift.
 //   * small batches (<= 1024 indices): one CTA, election in shared-memory
-//     hash tables, touched nodes listed per level and recomputed 32 per warp,
-//     levels separated by __syncthreads;
+//     hash tables; per level the touched nodes are listed (warp counts, then
+//     offsets) and recomputed 32 per warp; levels separated by __syncthreads;
 //   * larger batches: a co-resident grid, election with atomicMax on global
 //     claim words, levels separated by grid barriers; claims are reset by
 //     their owner in the phase that reads them, so the claim arrays are
@@ -139,6 +139,7 @@ constexpr int kHashBits = 11;
 constexpr int kHash = 1 << kHashBits;      // >= 2 * kSmallMax: load factor <= 1/2
 constexpr uint32_t kEmpty = 0xffffffffu;
 constexpr size_t kSmallDynSmem = (size_t)(kThreads / 32) * PER_NODE_TILE;
+constexpr int kSlotsPerWarp = kHash / (kThreads / 32);
 
 __device__ __forceinline__ uint32_t hslot(uint32_t key) {
   return (key * 2654435761u) >> (32 - kHashBits);
@@ -161,8 +162,8 @@ __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a
   __shared__ uint32_t s_wkey[kHash];    // slot -> leaf index
   __shared__ uint32_t s_wval[kHash];    // slot -> winning position + 1
   __shared__ uint32_t s_set[2][kHash];  // touched nodes of the current / next level
-  __shared__ uint32_t s_list[kSmallMax];
-  __shared__ uint32_t s_count;
+  __shared__ uint32_t s_list[kHash];  // the touched nodes of the current level
+  __shared__ int s_wcount[kThreads / 32];
   __shared__ uint32_t s_max;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -183,10 +184,7 @@ __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a
     s_set[0][k] = kEmpty;
     s_set[1][k] = kEmpty;
   }
-  if (threadIdx.x == 0) {
-    s_max = 0u;
-    s_count = 0u;
-  }
+  if (threadIdx.x == 0) s_max = 0u;
   __syncthreads();
 
   // P0: new priorities, winner election (largest position wins), max priority
@@ -230,28 +228,43 @@ __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a
   }
   __syncthreads();
 
-  // P2..: list the touched nodes, recompute them 32 per warp, collect parents
+  // P2..: list the touched nodes of the level (each warp counts its share of
+  // the hash slots, then writes them at its offset: no shared counters),
+  // recompute them 32 per warp, and insert their parents into the next set
   int cur = 0;
   for (int L = 1; L < t.num_levels; ++L) {
     uint32_t* set = s_set[cur];
     uint32_t* nxt = s_set[cur ^ 1];
     const bool more = L + 1 < t.num_levels;
-    for (int k = threadIdx.x; k < kHash; k += kThreads) {
+    int cnt = 0;
+#pragma unroll
+    for (int it = 0; it < kSlotsPerWarp / 32; ++it)
+      cnt += __popc(__ballot_sync(PER_FULL_MASK, set[warp * kSlotsPerWarp + it * 32 + lane] != kEmpty));
+    if (lane == 0) s_wcount[warp] = cnt;
+    __syncthreads();
+    int off = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) {
+      off += w < warp ? s_wcount[w] : 0;
+      total += s_wcount[w];
+    }
+#pragma unroll
+    for (int it = 0; it < kSlotsPerWarp / 32; ++it) {
+      const int k = warp * kSlotsPerWarp + it * 32 + lane;
       const uint32_t node = set[k];
-      if (node != kEmpty) s_list[atomicAdd(&s_count, 1u)] = node;
+      const uint32_t m = __ballot_sync(PER_FULL_MASK, node != kEmpty);
+      if (node != kEmpty) s_list[off + __popc(m & ((1u << lane) - 1u))] = node;
+      off += __popc(m);
       set[k] = kEmpty;
     }
     __syncthreads();
-    const int cnt = (int)s_count;
-    for (int base = warp * 32; base < cnt; base += kThreads) {
+    for (int base = warp * 32; base < total; base += kThreads) {
       const int k = base + lane;
-      const bool own = k < cnt;
+      const bool own = k < total;
       const int64_t node = own ? (int64_t)s_list[k] : 0;
       per_warp_recompute(t.levels[L - 1], t.levels[L], node, own, lane, tile);
       if (own && more) hset_insert(nxt, (uint32_t)(node >> PER_LOG_FANOUT));
     }
-    __syncthreads();
-    if (threadIdx.x == 0) s_count = 0u;
     __syncthreads();
     cur ^= 1;
   }
