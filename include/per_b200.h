@@ -158,6 +158,26 @@ int per_update_priorities(const per_store_t* store, const int64_t* idx,
 int per_add(const per_store_t* store, const per_field_t* fields,
             int32_t n_fields, int64_t n, void* stream);
 
+/* Allocation-free variant of per_update_priorities(), for callers that cannot
+ * allocate device memory (an application that fixes the library's device
+ * memory at start-up and forbids later allocations, or a latency-critical
+ * path where cudaMalloc would synchronise the device). No counterpart in the
+ * reference: triton-per allocates through PyTorch.
+ * The claim words and grid-barrier words that per_update_priorities() takes
+ * from store->claims and store->scratch come instead from a scratch array
+ * compiled into the library (PER_NOALLOC_SCRATCH_BYTES, held on every GPU
+ * that loads the library until exit); store->claims and store->scratch may be
+ * NULL. Stores of more than PER_NOALLOC_MAX_CAPACITY slots are rejected with
+ * PER_ERR_TOO_LARGE. The first call on a device resolves the array's device
+ * address (cudaGetSymbolAddress, with that device current): make it before
+ * any stream capture. Every call first clears, on `stream`, the words it uses;
+ * calls that overlap on the GPU share the array and race: serialise them.
+ * Calls no cudaMalloc, cudaFree or allocating library routine. */
+#define PER_NOALLOC_MAX_CAPACITY 1048576
+#define PER_NOALLOC_SCRATCH_BYTES 4346368
+int per_update_priorities_noalloc(const per_store_t* store, const int64_t* idx,
+                                  const float* td, int64_t n, void* stream);
+
 /* Recompute every tree level above the leaves from the leaves and clear the
  * claim scratch. Call after writing priorities directly.
  * Replaces the exact refresh of reference buffer.py:156-162. */

@@ -19,6 +19,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(PKG)), "include", "per_b20
 MAX_LEVELS = 7
 STATUS_WORDS = 16
 MAX_FIELDS = 16
+NOALLOC_MAX_CAPACITY = 1048576
 
 i64 = ctypes.c_int64
 i32 = ctypes.c_int32
@@ -90,6 +91,7 @@ SIGNATURES = {
     "per_update_priorities": (ctypes.c_int, [ctypes.POINTER(Store), vp, vp, i64, vp]),
     "per_add": (ctypes.c_int, [ctypes.POINTER(Store), ctypes.POINTER(Field), i32, i64, vp]),
     "per_rebuild_sums": (ctypes.c_int, [ctypes.POINTER(Store), vp]),
+    "per_update_priorities_noalloc": (ctypes.c_int, [ctypes.POINTER(Store), vp, vp, i64, vp]),
     "per_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "per_last_cuda_error": (ctypes.c_int, []),
     "per_abi_version": (ctypes.c_int, []),
