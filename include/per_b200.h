@@ -53,6 +53,7 @@ extern "C" {
 #define PER_STATUS_WORDS 16
 #define PER_MAX_GRID 4096  /* max CTAs of one grid-synchronised launch */
 #define PER_SCRATCH_BYTES (256 + 4 * PER_MAX_GRID)
+#define PER_MAX_SHARDS 64  /* shards of one sharded buffer */
 
 /* return codes */
 #define PER_OK 0
@@ -182,6 +183,41 @@ int per_update_priorities_noalloc(const per_store_t* store, const int64_t* idx,
  * claim scratch. Call after writing priorities directly.
  * Replaces the exact refresh of reference buffer.py:156-162. */
 int per_rebuild_sums(const per_store_t* store, void* stream);
+
+/* ---- sharded mode (no counterpart in the reference, which has no
+ * multi-GPU code). Shard g of `world` owns global slots
+ * [g * shard_capacity, (g + 1) * shard_capacity) in its own store. All shards
+ * draw the same global uniforms; a draw belongs to the shard whose range of
+ * the global priority prefix holds u = rand * total, so the union of the
+ * shards' draws equals the draw of one buffer holding every slot. */
+
+/* stats[0] = total priority of this shard (float64), stats[1] = its live
+ * size; the caller all-gathers these into a [world][2] array. */
+int per_shard_stats(const per_store_t* store, double* stats, void* stream);
+
+/* per_sample_fused() for shard `rank` of `world`: `stats` is the all-gathered
+ * [world][2] array, `rand` the `batch` global uniforms (identical on every
+ * shard). The draws this shard owns are searched, gathered and weighted with
+ * the global size and total, then compacted into out/idx/w/pos (pos = global
+ * draw position; the order of the compacted draws is unspecified); *count
+ * receives their number and *local_max their max unnormalised weight. The
+ * caller reduces local_max over the shards (max) and calls per_normalize().
+ * Replaces, per shard, reference buffer.py:82-105 and fused.py:16-52. */
+int per_sample_sharded(const per_store_t* store, int32_t rank, int32_t world,
+                       int64_t shard_base, const double* stats, const float* rand,
+                       int64_t batch, float beta, float* out, int64_t out_stride,
+                       int64_t* idx, float* w, int32_t* pos, int64_t* count,
+                       float* local_max, void* stream);
+
+/* w[j] /= *gmax for j < min(*count, cap) (device count and max). */
+int per_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap, void* stream);
+
+/* per_update_priorities() with global indices: slot = idx - base; indices
+ * owned by other shards (or negative padding) are skipped and counted in
+ * status[PER_STATUS_FOREIGN]. Replaces, per shard, reference
+ * buffer.py:133-162. */
+int per_update_priorities_shard(const per_store_t* store, int64_t base, const int64_t* idx,
+                                const float* td, int64_t n, void* stream);
 
 /* Human-readable name of a PER_* return code. */
 const char* per_error_string(int code);

@@ -264,6 +264,53 @@ int per_add(const per_store_t* store, const per_field_t* fields, int32_t n_field
   return per_launch_add(tree_of(store), fields, n_fields, n, (cudaStream_t)stream);
 }
 
+int per_shard_stats(const per_store_t* store, double* out, void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (!out) return PER_ERR_NULL_POINTER;
+  if (((uintptr_t)out) % 8) return PER_ERR_MISALIGNED;
+  return per_launch_shard_stats(tree_of(store), out, (cudaStream_t)stream);
+}
+
+int per_sample_sharded(const per_store_t* store, int32_t rank, int32_t world, int64_t shard_base,
+                       const double* stats, const float* rand, int64_t batch, float beta,
+                       float* out, int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
+                       int64_t* count, float* local_max, void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (!stats || !rand || !out || !idx || !w || !pos || !count || !local_max)
+    return PER_ERR_NULL_POINTER;
+  if (world < 1 || world > PER_MAX_SHARDS || rank < 0 || rank >= world || shard_base < 0)
+    return PER_ERR_INVALID_ARGUMENT;
+  if (batch < 1) return PER_ERR_EMPTY;
+  if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
+  if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4 ||
+      ((uintptr_t)stats) % 8 || ((uintptr_t)pos) % 4 || ((uintptr_t)count) % 8)
+    return PER_ERR_MISALIGNED;
+  return per_launch_sample_sharded(tree_of(store), rank, world, shard_base, stats, rand, batch,
+                                   beta, out, out_stride, idx, w, pos, count, local_max,
+                                   (cudaStream_t)stream);
+}
+
+int per_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap, void* stream) {
+  if (!w || !count || !gmax) return PER_ERR_NULL_POINTER;
+  if (cap < 0) return PER_ERR_INVALID_ARGUMENT;
+  if (cap == 0) return PER_OK;
+  return per_launch_normalize(w, count, gmax, cap, (cudaStream_t)stream);
+}
+
+int per_update_priorities_shard(const per_store_t* store, int64_t base, const int64_t* idx,
+                                const float* td, int64_t n, void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (!idx || !td) return PER_ERR_NULL_POINTER;
+  if (base < 0) return PER_ERR_INVALID_ARGUMENT;
+  if (n < 1) return PER_ERR_EMPTY;
+  if (n >= (int64_t)0xffffffffLL) return PER_ERR_TOO_LARGE;
+  return per_launch_update_shard(tree_of(store), base, 0, idx, td, n, (cudaStream_t)stream);
+}
+
 int per_rebuild_sums(const per_store_t* store, void* stream) {
   int rc = check_store(store);
   if (rc) return rc;

@@ -74,6 +74,13 @@ __device__ __forceinline__ uint32_t per_smem_addr_generic(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
 
+// Butterfly sum of one float64 per lane; every lane gets the same bits.
+__device__ __forceinline__ double per_warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 // Inclusive warp scan in float64.
 __device__ __forceinline__ double per_warp_scan_incl(double v, int lane) {
 #pragma unroll

@@ -30,6 +30,18 @@ int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float 
                       cudaStream_t stream);
 int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int64_t n,
                       cudaStream_t stream);
+// Update with global indices: slot = idx - base; indices outside the store
+// are errors when strict, else skipped and counted as another shard's.
+int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, const int64_t* idx,
+                            const float* td, int64_t n, cudaStream_t stream);
+int per_launch_sample_sharded(const PerTree& t, int32_t rank, int32_t world, int64_t shard_base,
+                              const double* stats, const float* rand, int64_t batch, float beta,
+                              float* out, int64_t out_stride, int64_t* idx, float* w,
+                              int32_t* pos, int64_t* count, float* local_max,
+                              cudaStream_t stream);
 int per_launch_add(const PerTree& t, const per_field_t* fields, int32_t n_fields, int64_t n,
                    cudaStream_t stream);
 int per_launch_rebuild(const PerTree& t, cudaStream_t stream);
+int per_launch_shard_stats(const PerTree& t, double* out, cudaStream_t stream);
+int per_launch_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap,
+                         cudaStream_t stream);

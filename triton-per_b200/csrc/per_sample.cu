@@ -62,6 +62,14 @@ struct SampleArgs {
   int32_t cp_bytes;        // cp.async piece size when not using bulk copies (4, 8, 16)
   int32_t pre_bytes;       // bytes of the padded prefix array
   int64_t num_tiles;
+  // sharded mode: this store is shard `rank` of `world` shards
+  const double* stats;           // [world][2] of every shard: total priority, live size
+  int32_t rank;
+  int32_t world;
+  int64_t shard_base;            // global index of this shard's slot 0
+  int32_t* pos;                  // global draw position of each compacted draw
+  unsigned long long* count;     // draws owned by this shard (compacted output length)
+  float* local_max;              // max unnormalised weight over this shard's draws
 };
 
 // Padded position of prefix entry i: one spare double every 32.
@@ -282,7 +290,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
 constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
 
-template <int VEC>
+template <int VEC, bool SHARDED>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(SampleArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ double s_wsum[kMaxWarps + 1];
@@ -411,6 +419,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
         __nanosleep(PER_SPIN_SLEEP_NS);
       }
       s_gmax = __uint_as_float(per_ld_relaxed_u32(&sc->mx_bits[gen & 1u]));
+      if (SHARDED && blockIdx.x == 0) *a.local_max = s_gmax;
     }
     __syncwarp();
     named_bar_arrive(kBarGmaxReady, nthreads);
@@ -418,9 +427,22 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   }
 
   // ---- compute warps
-  const double total64 = s_pre[ppos(n_top)];
+  // local total (this store); global total, size and this store's offset in
+  // the global prefix (sharded: summed over the shards in rank order)
+  const double ltotal64 = s_pre[ppos(n_top)];
+  double total64 = ltotal64, base64 = 0.0;
+  float sizef = (float)size;
+  if (SHARDED) {
+    double S = 0.0, N = 0.0;
+    for (int g = 0; g < a.world; ++g) {
+      if (g == a.rank) base64 = S;
+      S += __ldg(a.stats + 2 * g);
+      N += __ldg(a.stats + 2 * g + 1);
+    }
+    total64 = S;
+    sizef = __double2float_rn(N);
+  }
   const float total = __double2float_rn(total64);
-  const float sizef = (float)size;
   const float* leaves = t.levels[0];
   uint32_t n_fallback = 0, n_clamp = 0, n_zero = 0;
   uint32_t wmax_bits = 0u;
@@ -433,13 +455,35 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     const bool ok = j < a.batch;
     const float rnd = tile == blockIdx.x ? rnd0 : (ok ? __ldg(a.rand + j) : 0.f);
 
-    // top level: binary search of the staged prefix
     const float u = __fmul_rn(rnd, total);
     double r = (double)u;
+    bool own = ok;
+    unsigned long long obase = 0ull;  // sharded: first output slot of this warp's draws
+    uint32_t om = 0u;
+    if (SHARDED) {
+      // the shard whose range of the global prefix holds u (the last shard
+      // with mass if u is at or past the total)
+      double S = 0.0;
+      int owner = -1, lastpos = 0;
+      for (int g = 0; g < a.world; ++g) {
+        const double tg = __ldg(a.stats + 2 * g);
+        if (tg > 0.0) lastpos = g;
+        S += tg;
+        if (owner < 0 && S > r) owner = g;
+      }
+      if (owner < 0) owner = lastpos;
+      own = ok && owner == a.rank;
+      r -= base64;
+      om = __ballot_sync(PER_FULL_MASK, own);
+      if (lane == 0 && om) obase = atomicAdd(a.count, (unsigned long long)__popc(om));
+      obase = __shfl_sync(PER_FULL_MASK, obase, 0);
+    }
+
+    // top level: binary search of the staged prefix
     bool fb = false;
     int k = upper_bound_pre(s_pre, n_top, r);
-    if (k >= n_top) {  // u at or past the total: last node with mass
-      k = lower_bound_pre(s_pre, n_top, total64);
+    if (k >= n_top) {  // at or past the store's total: last node with mass
+      k = lower_bound_pre(s_pre, n_top, ltotal64);
       if (k >= n_top) k = n_top - 1;
       fb = true;
     }
@@ -470,8 +514,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
 
     int64_t i = node;
     float wv = 0.f;
-    if (ok) {
-      if (i > size - 1 || total64 <= 0.0) {  // sampling.py:49-51 clamp; p reloaded there
+    if (own) {
+      if (i > size - 1 || ltotal64 <= 0.0) {  // sampling.py:49-51 clamp; p reloaded there
         i = size - 1;
         p = __ldg(leaves + i);
         ++n_clamp;
@@ -501,7 +545,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       wmax_bits = max(wmax_bits, __float_as_uint(wv));
     }
     if (last_tile) {  // hand this warp's max to the helper warp and move on
-      w_last = wv;
+      if (!SHARDED) w_last = wv;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1)
         wmax_bits = max(wmax_bits, __shfl_xor_sync(PER_FULL_MASK, wmax_bits, o));
@@ -509,23 +553,39 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       __syncwarp();
       named_bar_arrive(kBarMaxReady, nthreads);
     }
-    if (ok) {
-      a.idx[j] = i;
-      if (!last_tile) a.w[j] = wv;
+    int64_t row0;  // first output row of this warp's gathered rows
+    int nrows;
+    if (SHARDED) {  // compact the owned draws into [obase, obase + popc(om))
+      const int orank = __popc(om & ((1u << lane) - 1u));
+      if (own) {
+        const unsigned long long slot = obase + orank;
+        a.idx[slot] = a.shard_base + i;
+        a.w[slot] = wv;
+        a.pos[slot] = (int32_t)j;
+        s_rows[warp][orank] = (int32_t)i;
+      }
+      row0 = (int64_t)obase;
+      nrows = __popc(om);
+    } else {
+      if (ok) {
+        a.idx[j] = i;
+        if (!last_tile) a.w[j] = wv;
+      }
+      s_rows[warp][lane] = (int32_t)i;
+      row0 = wj0;
+      nrows = (int)min((int64_t)32, a.batch - wj0);
     }
-    s_rows[warp][lane] = (int32_t)i;
     __syncwarp();
 
     // ---- gather this warp's rows
-    const int nrows = (int)min((int64_t)32, a.batch - wj0);
     if (a.rows_per_stage > 0) {
       for (int r0 = 0; r0 < nrows; r0 += a.rows_per_stage) {
         const int rn = min(a.rows_per_stage, nrows - r0);
         gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp]);
-        gather_finish<VEC>(a, stage, wj0 + r0, rn, lane, &s_mbar[warp], phase);
+        gather_finish<VEC>(a, stage, row0 + r0, rn, lane, &s_mbar[warp], phase);
       }
     } else if (nrows > 0) {
-      gather_direct<VEC>(a, s_rows[warp], wj0, nrows, lane);
+      gather_direct<VEC>(a, s_rows[warp], row0, nrows, lane);
     }
   }
 
@@ -535,7 +595,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     if (n_zero) per_count(t.status, PER_STATUS_ZERO_WALKS, n_zero);
   }
   // ---- normalise this warp's weights by the global max from the helper warp
+  // (sharded: the caller normalises after reducing the max over the shards)
   named_bar_sync(kBarGmaxReady, nthreads);
+  if (SHARDED) return;
   const float gmax = s_gmax;
   for (int64_t tl = blockIdx.x; tl < a.num_tiles; tl += gridDim.x) {
     const int64_t j = tl * tile_draws + warp * 32 + lane;
@@ -544,9 +606,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   }
 }
 
-template <int VEC>
+template <int VEC, bool SHARDED>
 int launch_vec(SampleArgs a, cudaStream_t stream) {
-  const void* fn = (const void*)per_sample_kernel<VEC>;
+  const void* fn = (const void*)per_sample_kernel<VEC, SHARDED>;
   // compute warps per CTA: spread small batches one warp per SM, up to 8
   int sms = 148;
   {
@@ -580,9 +642,10 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
 
 }  // namespace
 
-int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float beta, float* out,
-                      int64_t out_stride, int64_t* idx, float* w, cudaStream_t stream) {
-  SampleArgs a;
+namespace {
+
+void fill_common(SampleArgs& a, const PerTree& t, const float* rand, int64_t batch, float beta,
+                 float* out, int64_t out_stride, int64_t* idx, float* w) {
   a.t = t;
   a.rand = rand;
   a.batch = batch;
@@ -593,12 +656,13 @@ int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float 
   a.w = w;
   a.num_tiles = 0;
   a.pre_bytes = 0;
-  // widest vector that every row start and both bases allow
-  const uintptr_t al = (uintptr_t)t.storage | (uintptr_t)out | (uintptr_t)(t.row_stride * 4) |
-                       (uintptr_t)(out_stride * 4);
-  const int vec =
-      (al % 16 == 0 && t.row_dim % 4 == 0) ? 4 : (al % 8 == 0 && t.row_dim % 2 == 0) ? 2 : 1;
-  a.nvec = (int32_t)(t.row_dim / vec);
+  a.stats = nullptr;
+  a.rank = 0;
+  a.world = 1;
+  a.shard_base = 0;
+  a.pos = nullptr;
+  a.count = nullptr;
+  a.local_max = nullptr;
   // staged copies move whole pieces: 16 bytes when row starts and strides are
   // 16-byte aligned (rounding row_dim*4 up to 16 must stay inside the row
   // stride), else 8, else 4; bulk copies need the 16-byte case
@@ -624,7 +688,48 @@ int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float 
   }
   if (a.stage_bytes < kStageMin) a.stage_bytes = kStageMin;  // the level tiles share it
   a.stage_bytes = (a.stage_bytes + 15) & ~15;
-  if (vec == 4) return launch_vec<4>(a, stream);
-  if (vec == 2) return launch_vec<2>(a, stream);
-  return launch_vec<1>(a, stream);
+}
+
+// widest vector that every row start and both bases allow
+int vec_width(const PerTree& t, const float* out, int64_t out_stride) {
+  const uintptr_t al = (uintptr_t)t.storage | (uintptr_t)out | (uintptr_t)(t.row_stride * 4) |
+                       (uintptr_t)(out_stride * 4);
+  return (al % 16 == 0 && t.row_dim % 4 == 0) ? 4 : (al % 8 == 0 && t.row_dim % 2 == 0) ? 2 : 1;
+}
+
+template <bool SHARDED>
+int launch_any(SampleArgs& a, int vec, cudaStream_t stream) {
+  a.nvec = (int32_t)(a.t.row_dim / vec);
+  if (vec == 4) return launch_vec<4, SHARDED>(a, stream);
+  if (vec == 2) return launch_vec<2, SHARDED>(a, stream);
+  return launch_vec<1, SHARDED>(a, stream);
+}
+
+}  // namespace
+
+int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float beta, float* out,
+                      int64_t out_stride, int64_t* idx, float* w, cudaStream_t stream) {
+  SampleArgs a;
+  fill_common(a, t, rand, batch, beta, out, out_stride, idx, w);
+  return launch_any<false>(a, vec_width(t, out, out_stride), stream);
+}
+
+int per_launch_sample_sharded(const PerTree& t, int32_t rank, int32_t world, int64_t shard_base,
+                              const double* stats, const float* rand, int64_t batch, float beta,
+                              float* out, int64_t out_stride, int64_t* idx, float* w,
+                              int32_t* pos, int64_t* count, float* local_max,
+                              cudaStream_t stream) {
+  SampleArgs a;
+  fill_common(a, t, rand, batch, beta, out, out_stride, idx, w);
+  a.stats = stats;
+  a.rank = rank;
+  a.world = world;
+  a.shard_base = shard_base;
+  a.pos = pos;
+  a.count = reinterpret_cast<unsigned long long*>(count);
+  a.local_max = local_max;
+  cudaError_t e = cudaMemsetAsync(count, 0, sizeof(int64_t), stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(local_max, 0, sizeof(float), stream);
+  if (e != cudaSuccess) return per_record_cuda(e);
+  return launch_any<true>(a, vec_width(t, out, out_stride), stream);
 }

@@ -40,7 +40,14 @@ struct UpdateArgs {
   const int64_t* idx;
   const float* td;
   int64_t n;
+  int64_t base;    // global index of slot 0 (sharded stores); 0 otherwise
+  int32_t strict;  // 1: indices outside the store are errors; 0: another shard's (skipped)
 };
+
+// Slot of entry e in this store, or -1 (counted) if it is outside.
+__device__ __forceinline__ int64_t slot_of(const UpdateArgs& a, int64_t e) {
+  return a.idx[e] - a.base;
+}
 
 __device__ __forceinline__ float new_priority(const PerTree& t, float td) {
   return powf(fabsf(td) + t.eps, t.alpha);  // update.py:32, buffer.py:139
@@ -64,13 +71,13 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
   float* leaves = t.levels[0];
 
   // P0: new priorities, winner election (largest position wins), max priority
-  uint32_t active = 0u, tmax = 0u, nbad = 0u;
+  uint32_t active = 0u, tmax = 0u, nbad = 0u, nforeign = 0u;
   for (int q = 0; q < kMaxPerThread; ++q) {
     const int64_t e = tid + (int64_t)q * nth;
     if (e >= a.n) break;
-    const int64_t i = a.idx[e];
+    const int64_t i = slot_of(a, e);
     if (i < 0 || i >= t.capacity) {
-      ++nbad;
+      if (a.strict) ++nbad; else ++nforeign;
       continue;
     }
     tmax = max(tmax, __float_as_uint(new_priority(t, a.td[e])));
@@ -81,6 +88,7 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
     per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
     per_flag(t.status, PER_EVT_BAD_INDEX);
   }
+  if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
   if (lane == 0 && tmax) atomicMax(&s_max, tmax);
@@ -94,7 +102,7 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
   for (uint32_t m = active; m; m &= m - 1) {
     const int q = __ffs(m) - 1;
     const int64_t e = tid + (int64_t)q * nth;
-    const int64_t i = a.idx[e];
+    const int64_t i = slot_of(a, e);
     if (__ldcg(tags + i) == (uint32_t)(e + 1)) {
       tags[i] = 0u;
       leaves[i] = new_priority(t, a.td[e]);
@@ -118,7 +126,7 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
       bool own = false;
       int64_t node = 0;
       if ((active >> q) & 1u) {
-        node = a.idx[e] >> (PER_LOG_FANOUT * L);
+        node = slot_of(a, e) >> (PER_LOG_FANOUT * L);
         own = __ldcg(cl + node) == (uint32_t)(e + 1);
         if (own) cl[node] = 0u;
       }
@@ -175,7 +183,7 @@ __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a
 #pragma unroll
   for (int q = 0; q < kSmallPer; ++q) {
     const int64_t e = threadIdx.x + q * kThreads;
-    li[q] = e < a.n ? a.idx[e] : -1;
+    li[q] = e < a.n ? slot_of(a, e) : -1;
     tdv[q] = e < a.n ? a.td[e] : 0.f;
   }
   for (int k = threadIdx.x; k < kHash; k += kThreads) {
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a
   // P0: new priorities, winner election (largest position wins), max priority
   int slot[kSmallPer];
   float np[kSmallPer];
-  uint32_t tmax = 0u, nbad = 0u;
+  uint32_t tmax = 0u, nbad = 0u, nforeign = 0u;
 #pragma unroll
   for (int q = 0; q < kSmallPer; ++q) {
     const int64_t e = threadIdx.x + q * kThreads;
@@ -198,7 +206,7 @@ __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a
     np[q] = 0.f;
     if (e < a.n) {
       if (li[q] < 0 || li[q] >= t.capacity) {
-        ++nbad;
+        if (a.strict) ++nbad; else ++nforeign;
       } else {
         np[q] = new_priority(t, tdv[q]);
         tmax = max(tmax, __float_as_uint(np[q]));
@@ -211,6 +219,7 @@ __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a
     per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
     per_flag(t.status, PER_EVT_BAD_INDEX);
   }
+  if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
   if (lane == 0 && tmax) atomicMax(&s_max, tmax);
@@ -373,11 +382,18 @@ int grid_for(const void* fn, int64_t work, int* grid) {
 
 int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int64_t n,
                       cudaStream_t stream) {
+  return per_launch_update_shard(t, 0, 1, idx, td, n, stream);
+}
+
+int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, const int64_t* idx,
+                            const float* td, int64_t n, cudaStream_t stream) {
   UpdateArgs a;
   a.t = t;
   a.idx = idx;
   a.td = td;
   a.n = n;
+  a.base = base;
+  a.strict = strict;
   if (n <= kSmallMax) {
     const void* fs = (const void*)per_update_small_kernel;
     int rc = per_set_smem(fs, kSmallDynSmem);

@@ -92,6 +92,11 @@ SIGNATURES = {
     "per_add": (ctypes.c_int, [ctypes.POINTER(Store), ctypes.POINTER(Field), i32, i64, vp]),
     "per_rebuild_sums": (ctypes.c_int, [ctypes.POINTER(Store), vp]),
     "per_update_priorities_noalloc": (ctypes.c_int, [ctypes.POINTER(Store), vp, vp, i64, vp]),
+    "per_shard_stats": (ctypes.c_int, [ctypes.POINTER(Store), vp, vp]),
+    "per_sample_sharded": (ctypes.c_int, [ctypes.POINTER(Store), i32, i32, i64, vp, vp, i64,
+                                          ctypes.c_float, vp, i64, vp, vp, vp, vp, vp, vp]),
+    "per_normalize": (ctypes.c_int, [vp, vp, vp, i64, vp]),
+    "per_update_priorities_shard": (ctypes.c_int, [ctypes.POINTER(Store), i64, vp, vp, i64, vp]),
     "per_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "per_last_cuda_error": (ctypes.c_int, []),
     "per_abi_version": (ctypes.c_int, []),
