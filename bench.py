@@ -20,8 +20,17 @@ Metric: sampled transitions per second (sample + gather + IS weights).
             backend, C, all host threads) on a bounded sample of the same loop.
 
 --impl reference times that CPU implementation alone on the same loop.
-N>1 (torchrun): every rank runs an independent replica of the loop on its own
-GPU (no collective on the data path); value = all ranks' transitions / max time.
+
+N>1 (torchrun, one rank per GPU): the same loop weak-scaled over the sharded
+buffer: each rank holds a 1,000,000 x 74 shard (N x 1M slots in all), a step
+is add 1 per rank + 32 x (sharded sample of a global batch of N x 256 ->
+update of each rank's own draws); every sample exchanges the shard totals
+(all-gather) and the max weight (all-reduce) over NCCL. value = all ranks'
+transitions / max step time over ranks.
+
+--workload sharded64m: 64,000,000 x 74 slots split over the N ranks
+(lognormal(0,1) priorities), one step = sharded sample of a global batch of
+65,536 -> update of each rank's draws (strong scaling).
 """
 
 from __future__ import annotations
@@ -30,7 +39,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -70,63 +78,128 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during timing."""
+    """SM clock and clock-event (throttle) reasons of one GPU while the timed
+    region runs: NVML polled every 2 ms, else `nvidia-smi -lms 100` (reads
+    only; nothing is set)."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+    SMI_FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
-        self.t = None
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.source = "unavailable"
+        self.error = None
+        self._stop = threading.Event()
+        self._t = None
+        self._nvml = None
+        self._smi = None
+
+    def _nvml_handle(self, nv):
+        """The NVML device behind torch's cuda:<index> (UUID match, else the
+        CUDA_VISIBLE_DEVICES entry, else the same index)."""
+        try:
+            want = str(torch.cuda.get_device_properties(self.cuda_index).uuid).lower()
+            want = want.removeprefix("gpu-")
+            for i in range(nv.nvmlDeviceGetCount()):
+                h = nv.nvmlDeviceGetHandleByIndex(i)
+                u = nv.nvmlDeviceGetUUID(h)
+                u = (u.decode() if isinstance(u, bytes) else u).lower().removeprefix("gpu-")
+                if u == want:
+                    return h, i
+        except Exception:
+            pass
+        vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        if self.cuda_index < len(vis):
+            v = vis[self.cuda_index]
+            if v.isdigit():
+                return nv.nvmlDeviceGetHandleByIndex(int(v)), int(v)
+            return nv.nvmlDeviceGetHandleByUUID(v), None
+        return nv.nvmlDeviceGetHandleByIndex(self.cuda_index), self.cuda_index
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h, self._index = self._nvml_handle(pynvml)
+            self._nvml, self._h = pynvml, h
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.source = "nvml"
+            self._t = threading.Thread(target=self._poll, daemon=True)
+            self._t.start()
+        except Exception as e:  # no NVML: nvidia-smi in the background
+            self.error = repr(e)[:200]
+            self._nvml = None
+            self._start_smi()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _start_smi(self):
+        import subprocess
+
+        idx = self.cuda_index
+        vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        if idx < len(vis):
+            idx = vis[idx]
+        try:
+            self._smi = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(idx), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi"
+        except OSError as e:
+            self.error = repr(e)[:200]
+
+    def _poll(self):
+        nv, h = self._nvml, self._h
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                              getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+        while not self._stop.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                bits = int(get_reasons(h)) if get_reasons else 0
+                self.samples.append((mhz, bits))
+            except Exception as e:
+                self.error = repr(e)[:200]
+            self._stop.wait(0.002)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=2)
+        if self._smi is not None:
+            self._smi.terminate()
             try:
-                self.proc.wait(timeout=5)
+                out, _ = self._smi.communicate(timeout=5)
             except Exception:
-                self.proc.kill()
-            if self.t:
-                self.t.join(timeout=2)
+                self._smi.kill()
+                out = ""
+            for line in (out or "").splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                try:
+                    mhz, mx, bits = float(parts[0]), float(parts[1]), int(parts[2], 16)
+                except (ValueError, IndexError):
+                    continue
+                self.max_mhz = mx
+                self.samples.append((mhz, bits))
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+               "samples": len(self.samples), "source": self.source}
+        if self.error and not self.samples:
+            out["error"] = self.error
+        if not self.samples:
+            return out
+        reasons = set()
+        for _, bits in self.samples:
+            for b, name in self.REASONS.items():
+                if bits & b:
+                    reasons.add(name)
+        out["sm_mhz"] = statistics.median(m for m, _ in self.samples)
+        out["reasons"] = sorted(reasons)
+        return out
 
 
 # ---------------------------------------------------------------- distributed
@@ -207,7 +280,7 @@ def utd_step(buf, row, td):
         buf.update_priorities(idx, td[r])
 
 
-def capture(fn, warm=3):
+def capture(fn, warm=3, generators=()):
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -216,6 +289,8 @@ def capture(fn, warm=3):
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
+    for gen in generators:
+        g.register_generator_state(gen)
     with torch.cuda.graph(g):
         fn()
     torch.cuda.synchronize()
@@ -309,6 +384,173 @@ def e2e_loop(buf, steps, warmup, world, seed=9):
     barrier(world)
     ms = max_over_ranks(a.elapsed_time(b), world)
     return ms / steps, h2d, d2h
+
+
+# ---------------------------------------------------------------- sharded
+def make_sharded(device, rank, world, total_capacity, priorities, seed=1, exchange="auto"):
+    from per_b200.sharded import ShardedPERBuffer
+
+    sb = ShardedPERBuffer(total_capacity, FIELDS_74, device=device, seed=seed, exchange=exchange)
+    cap = sb.shard_capacity
+    buf = sb.shard.buf
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    chunk = 1_000_000
+    for s0 in range(0, cap, chunk):
+        n = min(chunk, cap - s0)
+        batch = {k: torch.randn(n, d, generator=g, device=device)
+                 for k, d in FIELDS_74.items() if k != "done"}
+        batch["done"] = (torch.rand(n, 1, generator=g, device=device) < 0.5).float()
+        buf.add(batch)
+    if priorities == "absnormal":
+        leaves = (torch.randn(cap, generator=g, device=device).abs() + 1e-6) ** 0.6
+    else:
+        leaves = torch.empty(cap, device=device).log_normal_(0.0, 1.0, generator=g)
+    buf.priorities[:cap] = leaves
+    buf.rebuild_sums()
+    torch.cuda.synchronize()
+    return sb
+
+
+def sharded_utd_step(sb, row, td, world):
+    sb.add(row)
+    for r in range(ROUNDS):
+        res = sb.sample(BATCH * world, BETA)
+        sb.update_priorities(res.idx, td[r])
+
+
+def sharded64m_step(sb, td, batch):
+    res = sb.sample(batch, BETA)
+    sb.update_priorities(res.idx, td)
+
+
+def time_eager(fn, iters, world):
+    st = torch.cuda.current_stream()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    a.record(st)
+    for _ in range(iters):
+        fn()
+    b.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    return a.elapsed_time(b)
+
+
+def run_sharded(args, world, rank, local):
+    """N>1 (or --workload sharded64m): the sharded buffer across the ranks."""
+    dev = torch.device("cuda", local)
+    big = args.workload == "sharded64m"
+    total_cap = 64_000_000 if big else CAPACITY * world
+    sb = make_sharded(dev, rank, world, total_cap, "lognormal" if big else "absnormal",
+                      exchange=args.exchange)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    gb = 65_536 if big else BATCH * world
+    td = torch.randn(ROUNDS, gb, generator=g, device=dev).abs()
+    row = {k: torch.randn(1, d, generator=g, device=dev) for k, d in FIELDS_74.items()}
+    p2p = sb.exchange == "p2p" and gb <= sb.p2p_max_batch
+    # kernels per sample+update (uniforms drawn inside the sample kernel): in-kernel
+    # exchange -> sample, update; collectives -> stats, sample, normalise, update
+    # (+ NCCL all-gather and all-reduce)
+    per_round = 2 if p2p else 4
+    if big:
+        fn = lambda: sharded64m_step(sb, td[0], gb)  # noqa: E731
+        per_step = gb
+        launches = per_round
+    else:
+        fn = lambda: sharded_utd_step(sb, row, td, world)  # noqa: E731
+        per_step = BATCH * world * ROUNDS
+        launches = 1 + ROUNDS * per_round
+    exchange_desc = ("shard totals and max weight exchanged inside the sample kernel over "
+                     "NVLink peer memory (CUDA IPC mailboxes)" if p2p else
+                     "NCCL all-gather of shard totals + all-reduce max per sample")
+    for _ in range(max(args.warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    # capture the step (kernels and NCCL collectives) into a CUDA graph; every
+    # rank must have captured before any rank replays, else all run eagerly
+    graph = None
+    try:
+        graph = capture(fn, warm=0)
+        ok = 1.0
+    except Exception as e:  # capture unsupported here: time the eager loop
+        graph = None
+        ok = 0.0
+        if rank == 0:
+            print(f"# graph capture failed, timing eagerly: {e!r}"[:300], file=sys.stderr)
+    ok = -max_over_ranks(-ok, world)  # min over ranks
+    if ok < 1.0:
+        graph = None
+    if graph is not None:
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+        mode = "CUDA graph of one step" + ("" if p2p else " (kernels + NCCL collectives)")
+        with ClockSampler(local) as clk:
+            ms = time_replays(graph, args.steps, world)
+    else:
+        mode = "eager (host-driven)"
+        with ClockSampler(local) as clk:
+            ms = time_eager(fn, args.steps, world)
+    ms = max_over_ranks(ms, world)
+    ms_per_step = ms / args.steps
+    value = per_step / (ms_per_step / 1e3)
+    st = sb.shard.buf.status()
+    bad = st["errors"] or st["timeouts"]
+    bad = max_over_ranks(float(bad), world)
+    if bad:
+        raise SystemExit(f"device status reports errors: {st}")
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if big else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {
+                "workload": ("sharded-64Mx74: sample 65536 beta 0.4 -> update own draws"
+                             if big else
+                             "sharded utd 1Mx74 per rank: add 1 + 32 x (sample 256/rank beta 0.4 "
+                             "-> update own draws)"),
+                "capacity_total": total_cap, "shard_capacity": sb.shard_capacity,
+                "row_dim": ROW_DIM, "global_batch": gb, "rounds": 1 if big else ROUNDS,
+                "parallelism": f"sharded x{world} ({exchange_desc})",
+                "l2": "rows (320 MB per 1M slots) exceed L2",
+                "timing": mode + ", CUDA events, max over ranks"},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk.summary(),
+        }
+    # e2e: the public API, eager, step inputs from pinned host memory and the
+    # sampled outputs back to pinned host memory
+    h_td = torch.abs(torch.randn(ROUNDS, gb)).pin_memory()
+    h_row = {k: torch.randn(1, d).pin_memory() for k, d in FIELDS_74.items()}
+    rounds = 1 if big else ROUNDS
+    h_out = torch.empty(rounds, gb, ROW_DIM).pin_memory()
+    h_idx = torch.empty(rounds, gb, dtype=torch.int64).pin_memory()
+    h_w = torch.empty(rounds, gb).pin_memory()
+
+    def e2e_step():
+        tdd = h_td.to(dev, non_blocking=True)
+        if not big:
+            sb.add({k: v.to(dev, non_blocking=True) for k, v in h_row.items()})
+        for r in range(rounds):
+            res = sb.sample(gb, BETA)
+            sb.update_priorities(res.idx, tdd[r])
+            h_out[r].copy_(torch.cat([res.views[k] for k in FIELDS_74], dim=1), non_blocking=True)
+            h_idx[r].copy_(res.idx, non_blocking=True)
+            h_w[r].copy_(res.w, non_blocking=True)
+
+    graph = None  # release graphs holding NCCL calls before the group is destroyed
+    for _ in range(3):
+        e2e_step()
+    e_ms = max_over_ranks(time_eager(e2e_step, max(3, min(args.steps, 20)), world), world)
+    e_ms /= max(3, min(args.steps, 20))
+    if rank == 0:
+        line["e2e"] = {"value": per_step / (e_ms / 1e3), "unit": UNIT,
+                       "h2d_bytes_per_step": h_td.numel() * 4 + (0 if big else ROW_DIM * 4),
+                       "d2h_bytes_per_step": rounds * gb * (ROW_DIM * 4 + 12)}
+        print(json.dumps(line), flush=True)
+    sb.close()
 
 
 # ---------------------------------------------------------------- CPU side
@@ -405,6 +647,9 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="utd", choices=["utd", "sharded64m"])
+    ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "nccl"],
+                    help="sharded mode: in-kernel peer-memory exchange or NCCL collectives")
     ap.add_argument("--kernel-only", type=int, default=0, metavar="BATCH",
                     help="profiling aid: eager fused samples of this batch (then updates of 256) "
                          "on the 1M x 74 store, no timing output")
@@ -432,6 +677,13 @@ def main():
         return
 
     world, rank, local = dist_setup(args)
+    if world > 1 or args.workload == "sharded64m":
+        run_sharded(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     dev = torch.device("cuda", local)
     buf = make_store(dev, seed=1 + rank)
     g = torch.Generator(device=dev).manual_seed(100 + rank)

@@ -54,6 +54,8 @@ extern "C" {
 #define PER_MAX_GRID 4096  /* max CTAs of one grid-synchronised launch */
 #define PER_SCRATCH_BYTES (256 + 4 * PER_MAX_GRID)
 #define PER_MAX_SHARDS 64  /* shards of one sharded buffer */
+#define PER_MAILBOX_BYTES 4096  /* peer-memory mailbox of one rank */
+#define PER_IPC_HANDLE_BYTES 64
 
 /* return codes */
 #define PER_OK 0
@@ -144,6 +146,16 @@ int per_sample_fused(const per_store_t* store, const float* rand, int64_t batch,
                      float beta, float* out, int64_t out_stride, int64_t* idx,
                      float* w, void* stream);
 
+/* per_sample_fused() with the uniforms drawn inside the kernel instead of
+ * read from `rand`: rand[j] = Philox4x32-10 (Salmon et al., SC 2011) with key
+ * `seed` and counter *counter + j (first output word, top 24 bits * 2^-24);
+ * the kernel then advances the device word *counter by `batch`, so repeated
+ * calls (and CUDA-graph replays) continue the stream. Replaces the
+ * torch.rand(batch) launch of reference buffer.py:85. */
+int per_sample_fused_rng(const per_store_t* store, uint64_t seed, uint64_t* counter,
+                         int64_t batch, float beta, float* out, int64_t out_stride,
+                         int64_t* idx, float* w, void* stream);
+
 /* p_i <- (|td_i| + eps)^alpha for every i, max-priority tracking, and exact
  * recomputation of every touched chunk / block / upper node. Duplicate
  * indices resolve deterministically: the last occurrence wins.
@@ -199,8 +211,9 @@ int per_shard_stats(const per_store_t* store, double* stats, void* stream);
  * [world][2] array, `rand` the `batch` global uniforms (identical on every
  * shard). The draws this shard owns are searched, gathered and weighted with
  * the global size and total, then compacted into out/idx/w/pos (pos = global
- * draw position; the order of the compacted draws is unspecified); *count
- * receives their number and *local_max their max unnormalised weight. The
+ * draw position; the order of the compacted draws is unspecified; idx
+ * entries past them are set to -1); *count receives their number and
+ * *local_max their max unnormalised weight. The
  * caller reduces local_max over the shards (max) and calls per_normalize().
  * Replaces, per shard, reference buffer.py:82-105 and fused.py:16-52. */
 int per_sample_sharded(const per_store_t* store, int32_t rank, int32_t world,
@@ -208,6 +221,54 @@ int per_sample_sharded(const per_store_t* store, int32_t rank, int32_t world,
                        int64_t batch, float beta, float* out, int64_t out_stride,
                        int64_t* idx, float* w, int32_t* pos, int64_t* count,
                        float* local_max, void* stream);
+
+/* per_sample_sharded() with in-kernel Philox uniforms (as per_sample_fused_rng;
+ * the same seed and counter on every shard give every shard the same draws). */
+int per_sample_sharded_rng(const per_store_t* store, int32_t rank, int32_t world,
+                           int64_t shard_base, const double* stats, uint64_t seed,
+                           uint64_t* counter, int64_t batch, float beta, float* out,
+                           int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
+                           int64_t* count, float* local_max, void* stream);
+
+/* Peer-memory exchange (one process per GPU, GPUs connected by NVLink):
+ * each rank creates one mailbox, exports it as a CUDA IPC handle, and maps the
+ * handles of all peers. per_mailbox_create also zeroes the mailbox. These are
+ * set-up / tear-down calls (they allocate and map device memory). */
+int per_mailbox_create(void** mailbox, void* ipc_handle);
+int per_mailbox_open(const void* ipc_handle, void** mailbox);
+int per_mailbox_close(void* peer_mailbox);
+int per_mailbox_destroy(void* mailbox);
+
+/* per_sample_sharded() with both exchanges done inside the kernel over peer
+ * memory instead of by the caller: the shard statistics and the max weight
+ * are written into slot `rank` of every rank's mailbox (`mailboxes`: a device
+ * array of `world` mailbox pointers as mapped in this process, own included)
+ * with system-scope release stores, and read back from this rank's mailbox
+ * after bounded waits; the weights come out normalised. Every rank must make
+ * the same sequence of calls (collective). batch must fit one wave of the
+ * kernel (PER_ERR_TOO_LARGE otherwise: use per_sample_sharded()). A peer that
+ * does not publish within about a second sets PER_EVT_PEER_TIMEOUT; the
+ * ranks' sequence numbers then disagree and the mailboxes must be destroyed
+ * and created again before the next call. The ranks' kernels wait on one
+ * another, so each rank must run on its own GPU. No counterpart in the
+ * reference (single GPU); the exchange it replaces is the host-side
+ * all-gather / all-reduce around per_sample_sharded(). */
+int per_sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world,
+                           int64_t shard_base, void* const* mailboxes, const float* rand,
+                           int64_t batch, float beta, float* out, int64_t out_stride,
+                           int64_t* idx, float* w, int32_t* pos, int64_t* count,
+                           void* stream);
+
+/* per_sample_sharded_p2p() with in-kernel Philox uniforms. */
+int per_sample_sharded_p2p_rng(const per_store_t* store, int32_t rank, int32_t world,
+                               int64_t shard_base, void* const* mailboxes, uint64_t seed,
+                               uint64_t* counter, int64_t batch, float beta, float* out,
+                               int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
+                               int64_t* count, void* stream);
+
+/* Largest batch per_sample_sharded_p2p() accepts for this store on the
+ * current device (one wave of co-resident CTAs, one tile per warp). */
+int per_sample_sharded_p2p_max_batch(const per_store_t* store, int64_t* max_batch);
 
 /* w[j] /= *gmax for j < min(*count, cap) (device count and max). */
 int per_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap, void* stream);

@@ -210,3 +210,40 @@ def classify_indices(idx_test, idx_oracle, rand, csum, size: int):
         b = csum[lo].astype(np.float64)
         excused = np.abs(u[diff].astype(np.float64) - b) <= ulp32(b)
     return int(it.size - diff.size), int(excused.sum()), diff[~excused]
+
+
+# ------------------------------------------------------------------ Philox
+PHILOX_M0, PHILOX_M1 = 0xD2511F53, 0xCD9E8D57
+PHILOX_W0, PHILOX_W1 = 0x9E3779B9, 0xBB67AE85
+
+
+def philox4x32_10(ctr: np.ndarray, key: tuple[int, int]) -> np.ndarray:
+    """Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
+    easy as 1, 2, 3", SC 2011) on uint32 counters ctr[..., 4]; returns the
+    uint32 outputs [..., 4]. Vectorised numpy restatement of the published
+    round function: two 32x32->64 products per round, keys bumped by the Weyl
+    constants. The engine's sample() uses it in place of the reference's
+    torch.rand (src/triton_per/buffer.py:85)."""
+    c = ctr.astype(np.uint64) & 0xFFFFFFFF
+    c0, c1, c2, c3 = c[..., 0], c[..., 1], c[..., 2], c[..., 3]
+    k0, k1 = np.uint64(key[0] & 0xFFFFFFFF), np.uint64(key[1] & 0xFFFFFFFF)
+    mask = np.uint64(0xFFFFFFFF)
+    for _ in range(10):
+        p0 = np.uint64(PHILOX_M0) * c0
+        p1 = np.uint64(PHILOX_M1) * c2
+        c0, c1, c2, c3 = ((p1 >> np.uint64(32)) ^ c1 ^ k0, p1 & mask,
+                          (p0 >> np.uint64(32)) ^ c3 ^ k1, p0 & mask)
+        k0 = (k0 + np.uint64(PHILOX_W0)) & mask
+        k1 = (k1 + np.uint64(PHILOX_W1)) & mask
+    return np.stack([c0, c1, c2, c3], axis=-1).astype(np.uint32)
+
+
+def philox_uniforms(seed: int, start: int, n: int) -> np.ndarray:
+    """Uniform j of the engine's stream `seed`: counter (lo(j), hi(j), 0, 0),
+    key (lo(seed), hi(seed)), top 24 bits of output word 0 times 2^-24."""
+    j = np.arange(start, start + n, dtype=np.uint64)
+    ctr = np.zeros((n, 4), np.uint64)
+    ctr[:, 0] = j & np.uint64(0xFFFFFFFF)
+    ctr[:, 1] = j >> np.uint64(32)
+    out = philox4x32_10(ctr, (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))
+    return ((out[:, 0] >> 8).astype(np.float32) * np.float32(2.0 ** -24)).astype(np.float32)

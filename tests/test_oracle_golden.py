@@ -125,3 +125,22 @@ def test_classifier_excuses_only_boundary_ties():
     wrong = np.minimum(idx + 1, cap - 1)
     _, _, bad2 = oracle.classify_indices(wrong, idx, c["rand"], csum, cap)
     assert bad2.size > 1000
+
+
+def test_philox_known_answers():
+    """The oracle's Philox4x32-10 against the published known-answer vectors
+    of the generator's authors (Random123 kat_vectors: zero, all-ones and pi
+    digits counter/key)."""
+    from oracle import oracle
+
+    kat = [
+        ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+        ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+        ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+         (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+    ]
+    for ctr, key, want in kat:
+        got = oracle.philox4x32_10(np.array([ctr], np.uint64), key)[0]
+        assert tuple(int(x) for x in got) == want
+    u = oracle.philox_uniforms(12345, 2**32 - 3, 10)  # counter crosses the 32-bit boundary
+    assert u.dtype == np.float32 and ((u >= 0) & (u < 1)).all()

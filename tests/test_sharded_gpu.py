@@ -131,3 +131,34 @@ def test_update_with_global_indices_touches_only_owned_slots():
         s = sh.buf.status()
         own = ((idx >= g * shard_cap) & (idx < (g + 1) * shard_cap)).sum()
         assert s["foreign"] == idx.size - own and s["bad_indices"] == 0
+
+
+def test_single_rank_p2p_exchange_equals_single_buffer():
+    """World 1 through the in-kernel exchange (the rank's own mailbox): the
+    draws, rows and weights equal PERBuffer.sample_from_uniforms bit for bit,
+    over several calls in a row and past the one-wave limit (collective path)."""
+    from per_b200.sharded import ShardedPERBuffer
+
+    rng = np.random.default_rng(17)
+    cap = 120_000
+    leaves = rng.lognormal(0.0, 1.0, cap).astype(np.float32)
+    rows = rng.standard_normal((cap, 7), dtype=np.float32)
+    ref = make_buffer(cap, {"x": 7}, {"x": rows}, leaves)
+    sb = ShardedPERBuffer(cap, {"x": 7}, device="cuda", exchange="p2p")
+    assert sb.exchange == "p2p" and sb.p2p_max_batch >= 148 * 32
+    sb.shard.buf.add({"x": torch.from_numpy(rows).cuda()})
+    sb.shard.buf.priorities[:cap] = torch.from_numpy(leaves).cuda()
+    sb.shard.buf.rebuild_sums()
+    for k, bs in enumerate((4096, 33, 65_536, sb.p2p_max_batch, sb.p2p_max_batch + 1)):
+        rand = torch.from_numpy(rng.random(bs, dtype=np.float32)).cuda()
+        views, idx, w = ref.sample_from_uniforms(rand, 0.4)
+        res = sb.sample_from_uniforms(rand, 0.4)
+        assert int(res.count.item()) == bs
+        assert torch.equal(torch.sort(res.pos.long()).values, torch.arange(bs, device="cuda"))
+        order = torch.argsort(res.pos.long())
+        assert torch.equal(res.idx[order], idx), k
+        assert torch.equal(res.w[order], w), k
+        assert torch.equal(res.views["x"][order], views["x"]), k
+    st = sb.shard.buf.status()
+    assert st["errors"] == 0 and st["timeouts"] == 0
+    sb.close()

@@ -219,18 +219,86 @@ int per_layout(int64_t capacity, per_layout_t* out) {
   return PER_OK;
 }
 
-int per_sample_fused(const per_store_t* store, const float* rand, int64_t batch, float beta,
-                     float* out, int64_t out_stride, int64_t* idx, float* w, void* stream) {
+namespace {
+
+// rand XOR rng: caller-provided uniforms, or the in-kernel Philox stream
+int sample_fused(const per_store_t* store, const float* rand, const PerRng* rng, int64_t batch,
+                 float beta, float* out, int64_t out_stride, int64_t* idx, float* w,
+                 void* stream) {
   int rc = check_store(store);
   if (rc) return rc;
-  if (!rand || !out || !idx || !w) return PER_ERR_NULL_POINTER;
+  if ((!rand && !rng) || !out || !idx || !w) return PER_ERR_NULL_POINTER;
+  if (rng && !rng->counter) return PER_ERR_NULL_POINTER;
   if (batch < 1) return PER_ERR_EMPTY;
   if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
   if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
-  if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4)
+  if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4 ||
+      (rng && ((uintptr_t)rng->counter) % 8))
     return PER_ERR_MISALIGNED;
-  return per_launch_sample(tree_of(store), rand, batch, beta, out, out_stride, idx, w,
+  return per_launch_sample(tree_of(store), rand, rng, batch, beta, out, out_stride, idx, w,
                            (cudaStream_t)stream);
+}
+
+int sample_sharded(const per_store_t* store, int32_t rank, int32_t world, int64_t shard_base,
+                   const double* stats, const float* rand, const PerRng* rng, int64_t batch,
+                   float beta, float* out, int64_t out_stride, int64_t* idx, float* w,
+                   int32_t* pos, int64_t* count, float* local_max, void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (!stats || (!rand && !rng) || !out || !idx || !w || !pos || !count || !local_max)
+    return PER_ERR_NULL_POINTER;
+  if (rng && !rng->counter) return PER_ERR_NULL_POINTER;
+  if (world < 1 || world > PER_MAX_SHARDS || rank < 0 || rank >= world || shard_base < 0)
+    return PER_ERR_INVALID_ARGUMENT;
+  if (batch < 1) return PER_ERR_EMPTY;
+  if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
+  if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4 ||
+      ((uintptr_t)stats) % 8 || ((uintptr_t)pos) % 4 || ((uintptr_t)count) % 8 ||
+      (rng && ((uintptr_t)rng->counter) % 8))
+    return PER_ERR_MISALIGNED;
+  return per_launch_sample_sharded(tree_of(store), rank, world, shard_base, stats, rand, rng,
+                                   batch, beta, out, out_stride, idx, w, pos, count, local_max,
+                                   (cudaStream_t)stream);
+}
+
+int sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world, int64_t shard_base,
+                       void* const* mailboxes, const float* rand, const PerRng* rng, int64_t batch,
+                       float beta, float* out, int64_t out_stride, int64_t* idx, float* w,
+                       int32_t* pos, int64_t* count, void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (!mailboxes || (!rand && !rng) || !out || !idx || !w || !pos || !count)
+    return PER_ERR_NULL_POINTER;
+  if (rng && !rng->counter) return PER_ERR_NULL_POINTER;
+  if (world < 1 || world > PER_MAX_SHARDS || rank < 0 || rank >= world || shard_base < 0)
+    return PER_ERR_INVALID_ARGUMENT;
+  if (batch < 1) return PER_ERR_EMPTY;
+  if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
+  if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4 ||
+      ((uintptr_t)pos) % 4 || ((uintptr_t)count) % 8 || ((uintptr_t)mailboxes) % 8 ||
+      (rng && ((uintptr_t)rng->counter) % 8))
+    return PER_ERR_MISALIGNED;
+  return per_launch_sample_sharded_p2p(tree_of(store), rank, world, shard_base,
+                                       reinterpret_cast<PerMailbox* const*>(mailboxes), rand, rng,
+                                       batch, beta, out, out_stride, idx, w, pos, count,
+                                       (cudaStream_t)stream);
+}
+
+}  // namespace
+
+int per_sample_fused(const per_store_t* store, const float* rand, int64_t batch, float beta,
+                     float* out, int64_t out_stride, int64_t* idx, float* w, void* stream) {
+  if (!rand) return PER_ERR_NULL_POINTER;
+  return sample_fused(store, rand, nullptr, batch, beta, out, out_stride, idx, w, stream);
+}
+
+int per_sample_fused_rng(const per_store_t* store, uint64_t seed, uint64_t* counter, int64_t batch,
+                         float beta, float* out, int64_t out_stride, int64_t* idx, float* w,
+                         void* stream) {
+  const PerRng rng{(unsigned long long)seed, reinterpret_cast<unsigned long long*>(counter)};
+  return sample_fused(store, nullptr, &rng, batch, beta, out, out_stride, idx, w, stream);
 }
 
 int per_update_priorities(const per_store_t* store, const int64_t* idx, const float* td, int64_t n,
@@ -276,21 +344,81 @@ int per_sample_sharded(const per_store_t* store, int32_t rank, int32_t world, in
                        const double* stats, const float* rand, int64_t batch, float beta,
                        float* out, int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
                        int64_t* count, float* local_max, void* stream) {
+  if (!rand) return PER_ERR_NULL_POINTER;
+  return sample_sharded(store, rank, world, shard_base, stats, rand, nullptr, batch, beta, out,
+                        out_stride, idx, w, pos, count, local_max, stream);
+}
+
+int per_sample_sharded_rng(const per_store_t* store, int32_t rank, int32_t world,
+                           int64_t shard_base, const double* stats, uint64_t seed,
+                           uint64_t* counter, int64_t batch, float beta, float* out,
+                           int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
+                           int64_t* count, float* local_max, void* stream) {
+  const PerRng rng{(unsigned long long)seed, reinterpret_cast<unsigned long long*>(counter)};
+  return sample_sharded(store, rank, world, shard_base, stats, nullptr, &rng, batch, beta, out,
+                        out_stride, idx, w, pos, count, local_max, stream);
+}
+
+int per_mailbox_create(void** mailbox, void* ipc_handle) {
+  if (!mailbox || !ipc_handle) return PER_ERR_NULL_POINTER;
+  static_assert(sizeof(cudaIpcMemHandle_t) == PER_IPC_HANDLE_BYTES, "ipc handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, PER_MAILBOX_BYTES);
+  if (e != cudaSuccess) return per_record_cuda(e);
+  e = cudaMemset(p, 0, PER_MAILBOX_BYTES);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return per_record_cuda(e);
+  }
+  *mailbox = p;
+  return PER_OK;
+}
+
+int per_mailbox_open(const void* ipc_handle, void** mailbox) {
+  if (!mailbox || !ipc_handle) return PER_ERR_NULL_POINTER;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(mailbox, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+}
+
+int per_mailbox_close(void* peer_mailbox) {
+  if (!peer_mailbox) return PER_ERR_NULL_POINTER;
+  cudaError_t e = cudaIpcCloseMemHandle(peer_mailbox);
+  return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+}
+
+int per_mailbox_destroy(void* mailbox) {
+  if (!mailbox) return PER_ERR_NULL_POINTER;
+  cudaError_t e = cudaFree(mailbox);
+  return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+}
+
+int per_sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world,
+                           int64_t shard_base, void* const* mailboxes, const float* rand,
+                           int64_t batch, float beta, float* out, int64_t out_stride,
+                           int64_t* idx, float* w, int32_t* pos, int64_t* count, void* stream) {
+  if (!rand) return PER_ERR_NULL_POINTER;
+  return sample_sharded_p2p(store, rank, world, shard_base, mailboxes, rand, nullptr, batch, beta,
+                            out, out_stride, idx, w, pos, count, stream);
+}
+
+int per_sample_sharded_p2p_rng(const per_store_t* store, int32_t rank, int32_t world,
+                               int64_t shard_base, void* const* mailboxes, uint64_t seed,
+                               uint64_t* counter, int64_t batch, float beta, float* out,
+                               int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
+                               int64_t* count, void* stream) {
+  const PerRng rng{(unsigned long long)seed, reinterpret_cast<unsigned long long*>(counter)};
+  return sample_sharded_p2p(store, rank, world, shard_base, mailboxes, nullptr, &rng, batch, beta,
+                            out, out_stride, idx, w, pos, count, stream);
+}
+
+int per_sample_sharded_p2p_max_batch(const per_store_t* store, int64_t* max_batch) {
   int rc = check_store(store);
   if (rc) return rc;
-  if (!stats || !rand || !out || !idx || !w || !pos || !count || !local_max)
-    return PER_ERR_NULL_POINTER;
-  if (world < 1 || world > PER_MAX_SHARDS || rank < 0 || rank >= world || shard_base < 0)
-    return PER_ERR_INVALID_ARGUMENT;
-  if (batch < 1) return PER_ERR_EMPTY;
-  if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
-  if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
-  if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4 ||
-      ((uintptr_t)stats) % 8 || ((uintptr_t)pos) % 4 || ((uintptr_t)count) % 8)
-    return PER_ERR_MISALIGNED;
-  return per_launch_sample_sharded(tree_of(store), rank, world, shard_base, stats, rand, batch,
-                                   beta, out, out_stride, idx, w, pos, count, local_max,
-                                   (cudaStream_t)stream);
+  if (!max_batch) return PER_ERR_NULL_POINTER;
+  return per_launch_sample_p2p_max_batch(tree_of(store), max_batch);
 }
 
 int per_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap, void* stream) {

@@ -14,6 +14,10 @@
 // reports PER_EVT_BARRIER_TIMEOUT instead of hanging the GPU.
 #define PER_SPIN_LIMIT (1u << 22)
 #define PER_SPIN_SLEEP_NS 32
+// Waits on another GPU (a peer rank's kernel, launched by another process)
+// are bounded by time: 1 s on the global timer, and at most 2^26 polls.
+#define PER_PEER_WAIT_NS 1000000000ull
+#define PER_PEER_SPIN_LIMIT (1u << 26)
 
 // Layout of store->scratch (PER_SCRATCH_BYTES).
 struct PerScratch {
@@ -22,10 +26,45 @@ struct PerScratch {
   uint32_t mx_count;     // sample: warps that published their max weight
   uint32_t mx_gen;       // sample: generation, bumped when every warp has published
   uint32_t mx_bits[2];   // sample: running max weight bits, by generation parity
-  uint32_t pad[58];      // keep partial[] 256-byte aligned
+  unsigned long long draws[2];  // sharded sample: owned-draw counter, by generation parity
+  uint32_t pad[54];      // keep partial[] 256-byte aligned
   float partial[PER_MAX_GRID];
 };
 static_assert(sizeof(PerScratch) == PER_SCRATCH_BYTES, "scratch layout");
+
+// Sharded mode, exchange over peer memory: every rank owns one mailbox,
+// mapped into every peer's process. Rank g writes its shard statistics and
+// its max weight into slot g of every mailbox; each rank reads only its own
+// mailbox. Every 64-bit word carries 32 bits of data and the 32-bit tag of
+// the call it belongs to (one single-copy-atomic store: no fence on either
+// side), and a reader waits until every word of a slot carries this call's
+// tag.
+struct PerMailbox {
+  unsigned long long seq;  // sample calls completed by the owning rank (local)
+  unsigned long long pad0[15];
+  unsigned long long stats[PER_MAX_SHARDS][4];  // slot g: total (2 halves), size (2 halves)
+  unsigned long long max_w[PER_MAX_SHARDS];     // slot g: max weight bits
+};
+static_assert(sizeof(PerMailbox) <= PER_MAILBOX_BYTES, "mailbox layout");
+
+// tag of call `seq` (never 0, the value of a fresh mailbox)
+__device__ __forceinline__ uint32_t per_mail_tag(unsigned long long seq) {
+  return (uint32_t)(seq & 0x7fffffffull) | 0x80000000u;
+}
+
+__device__ __forceinline__ void per_st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long per_ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void per_mail_put(unsigned long long* p, uint32_t data, uint32_t tag) {
+  per_st_relaxed_sys_u64(p, ((unsigned long long)tag << 32) | data);
+}
 
 __device__ __forceinline__ uint32_t per_ld_acquire(const uint32_t* p) {
   uint32_t v;
@@ -62,6 +101,44 @@ __device__ __forceinline__ void per_count(uint32_t* status, int word, uint32_t n
 
 __device__ __forceinline__ void per_flag(uint32_t* status, uint32_t bit) {
   if (status) atomicOr(status + PER_STATUS_ERRORS, bit);
+}
+
+__device__ __forceinline__ unsigned long long per_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ unsigned long long per_ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until the mailbox words p[0..n) all carry `tag`; returns their
+// data halves in out[]. False and a flagged peer timeout if the peer does not
+// publish within PER_PEER_WAIT_NS (a rank that left the collective, or one
+// far behind).
+__device__ __forceinline__ bool per_mail_get(const unsigned long long* p, int n, uint32_t tag,
+                                             uint32_t* out, uint32_t* status) {
+  unsigned long long t0 = 0ull;
+  for (uint32_t it = 0;; ++it) {
+    bool ready = true;
+    for (int k = 0; k < n; ++k) {
+      const unsigned long long v = per_ld_relaxed_sys_u64(p + k);
+      out[k] = (uint32_t)v;
+      ready &= (uint32_t)(v >> 32) == tag;
+    }
+    if (ready) return true;
+    if (it == 0) t0 = per_globaltimer();
+    if (it > PER_PEER_SPIN_LIMIT ||
+        ((it & 255u) == 255u && per_globaltimer() - t0 > PER_PEER_WAIT_NS)) {
+      per_flag(status, PER_EVT_PEER_TIMEOUT);
+      per_count(status, PER_STATUS_TIMEOUTS);
+      return false;
+    }
+    __nanosleep(PER_SPIN_SLEEP_NS);
+  }
 }
 
 // Positive floats order like their bit patterns, so max over non-negative
@@ -313,4 +390,40 @@ __device__ __forceinline__ void per_bulk_load(void* sdst, const void* gsrc, uint
           per_smem_addr(sdst)),
       "l"(gsrc), "r"(bytes), "r"(per_smem_addr(bar))
       : "memory");
+}
+
+// Philox4x32-10 counter-based generator (Salmon, Moraes, Dror, Shaw,
+// "Parallel random numbers: as easy as 1, 2, 3", SC 2011): 10 rounds of two
+// 32x32->64 multiplies with the round keys bumped by the Weyl constants.
+// Draw j of a stream uses counter (lo(j), hi(j), 0, 0) and key (lo(seed),
+// hi(seed)); its uniform is the top 24 bits of the first output word times
+// 2^-24, in [0, 1).
+#define PER_PHILOX_M0 0xD2511F53u
+#define PER_PHILOX_M1 0xCD9E8D57u
+#define PER_PHILOX_W0 0x9E3779B9u
+#define PER_PHILOX_W1 0xBB67AE85u
+
+__host__ __device__ __forceinline__ void per_philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)PER_PHILOX_M0 * c[0];
+    const uint64_t p1 = (uint64_t)PER_PHILOX_M1 * c[2];
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+    const uint32_t n1 = (uint32_t)p1;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+    const uint32_t n3 = (uint32_t)p0;
+    c[0] = n0;
+    c[1] = n1;
+    c[2] = n2;
+    c[3] = n3;
+    k0 += PER_PHILOX_W0;
+    k1 += PER_PHILOX_W1;
+  }
+}
+
+__host__ __device__ __forceinline__ float per_philox_uniform(unsigned long long seed,
+                                                             unsigned long long j) {
+  uint32_t c[4] = {(uint32_t)j, (uint32_t)(j >> 32), 0u, 0u};
+  per_philox4x32_10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+  return (float)(c[0] >> 8) * 5.9604644775390625e-08f;  // 2^-24
 }

@@ -25,8 +25,16 @@ int per_set_smem(const void* fn, size_t smem);
 cudaError_t per_launch(const void* fn, unsigned grid, unsigned threads, size_t smem,
                        cudaStream_t stream, void** args, bool grid_sync);
 
-int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float beta,
-                      float* out, int64_t out_stride, int64_t* idx, float* w,
+// In-kernel uniforms: Philox4x32-10 stream `seed`, position in *counter
+// (device), advanced by the kernel by the batch size.
+struct PerRng {
+  unsigned long long seed;
+  unsigned long long* counter;
+};
+
+// rng == nullptr: uniforms from `rand`
+int per_launch_sample(const PerTree& t, const float* rand, const PerRng* rng, int64_t batch,
+                      float beta, float* out, int64_t out_stride, int64_t* idx, float* w,
                       cudaStream_t stream);
 int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int64_t n,
                       cudaStream_t stream);
@@ -35,13 +43,19 @@ int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int
 int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, const int64_t* idx,
                             const float* td, int64_t n, cudaStream_t stream);
 int per_launch_sample_sharded(const PerTree& t, int32_t rank, int32_t world, int64_t shard_base,
-                              const double* stats, const float* rand, int64_t batch, float beta,
-                              float* out, int64_t out_stride, int64_t* idx, float* w,
-                              int32_t* pos, int64_t* count, float* local_max,
-                              cudaStream_t stream);
+                              const double* stats, const float* rand, const PerRng* rng,
+                              int64_t batch, float beta, float* out, int64_t out_stride,
+                              int64_t* idx, float* w, int32_t* pos, int64_t* count,
+                              float* local_max, cudaStream_t stream);
 int per_launch_add(const PerTree& t, const per_field_t* fields, int32_t n_fields, int64_t n,
                    cudaStream_t stream);
 int per_launch_rebuild(const PerTree& t, cudaStream_t stream);
 int per_launch_shard_stats(const PerTree& t, double* out, cudaStream_t stream);
+int per_launch_sample_p2p_max_batch(const PerTree& t, int64_t* max_batch);
+int per_launch_sample_sharded_p2p(const PerTree& t, int32_t rank, int32_t world,
+                                  int64_t shard_base, PerMailbox* const* mailboxes,
+                                  const float* rand, const PerRng* rng, int64_t batch, float beta,
+                                  float* out, int64_t out_stride, int64_t* idx, float* w,
+                                  int32_t* pos, int64_t* count, cudaStream_t stream);
 int per_launch_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap,
                          cudaStream_t stream);

@@ -70,7 +70,19 @@ struct SampleArgs {
   int32_t* pos;                  // global draw position of each compacted draw
   unsigned long long* count;     // draws owned by this shard (compacted output length)
   float* local_max;              // max unnormalised weight over this shard's draws
+  PerMailbox* const* mailboxes;  // exchange over peer memory: every rank's mailbox
+  int32_t p2p;                   // 1: exchange stats and max in-kernel through the mailboxes
+  // uniforms from the in-kernel Philox stream instead of `rand`
+  int32_t use_rng;
+  unsigned long long rng_seed;
+  unsigned long long* rng_counter;  // device: draws consumed so far (advanced by the kernel)
 };
+
+__device__ __forceinline__ float draw_uniform(const SampleArgs& a, unsigned long long cbase,
+                                              int64_t j) {
+  return a.use_rng ? per_philox_uniform(a.rng_seed, cbase + (unsigned long long)j)
+                   : __ldg(a.rand + j);
+}
 
 // Padded position of prefix entry i: one spare double every 32.
 __device__ __forceinline__ int ppos(int i) { return i + (i >> 5); }
@@ -298,6 +310,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   __shared__ uint64_t s_mbar[kMaxWarps];
   __shared__ uint32_t s_cta_max;
   __shared__ float s_gmax;
+  __shared__ double s_stats[SHARDED ? PER_MAX_SHARDS : 1][2];
+  __shared__ unsigned long long s_seq;
+  __shared__ unsigned long long s_owned;  // sharded: draws owned by this rank, all CTAs
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -318,13 +333,16 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   }
 
   // early, independent loads: generation of the max exchange, size, first uniform
-  const uint32_t gen = helper && lane == 0 ? per_ld_relaxed_u32(&sc->mx_gen) : 0u;
+  const uint32_t gen = SHARDED || (helper && lane == 0) ? per_ld_relaxed_u32(&sc->mx_gen) : 0u;
   const int64_t size = __ldg(t.size_cursor);
+  // every CTA reads the stream position before it arrives at the max exchange;
+  // CTA 0 advances it after the exchange has completed
+  const unsigned long long cbase = a.use_rng ? per_ld_relaxed_u64(a.rng_counter) : 0ull;
   int64_t tile = blockIdx.x;
   float rnd0 = 0.f;
   if (!helper) {
     const int64_t j = tile * tile_draws + threadIdx.x;
-    if (tile < a.num_tiles && j < a.batch) rnd0 = __ldg(a.rand + j);
+    if (tile < a.num_tiles && j < a.batch) rnd0 = draw_uniform(a, cbase, j);
   }
 
   // ---- prologue (all warps): float64 exclusive prefix of the top level
@@ -391,7 +409,40 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     if (end == nv4 && end > beg) s_pre[ppos(n_top)] = run;
     __syncthreads();
   }
-  if (size <= 0) {  // host checks first; keep the device consistent anyway
+  const double* stats = a.stats;
+  if (SHARDED && a.p2p) {
+    // ---- exchange the shard statistics over peer memory: CTA 0 publishes
+    // this shard's (total, size) into slot `rank` of every rank's mailbox;
+    // every CTA waits for all slots of its own mailbox to reach this call
+    PerMailbox* mine = a.mailboxes[a.rank];
+    if (threadIdx.x == 0) s_seq = *(volatile unsigned long long*)&mine->seq + 1ull;
+    __syncthreads();
+    const uint32_t tag = per_mail_tag(s_seq);
+    if (warp == 0) {
+      if (blockIdx.x == 0) {
+        const double tot = s_pre[ppos(n_top)];
+        const double szd = (double)size;
+        const unsigned long long tb = (unsigned long long)__double_as_longlong(tot);
+        const unsigned long long sb = (unsigned long long)__double_as_longlong(szd);
+        for (int g = lane; g < a.world; g += 32) {
+          unsigned long long* slot = a.mailboxes[g]->stats[a.rank];
+          per_mail_put(slot + 0, (uint32_t)tb, tag);
+          per_mail_put(slot + 1, (uint32_t)(tb >> 32), tag);
+          per_mail_put(slot + 2, (uint32_t)sb, tag);
+          per_mail_put(slot + 3, (uint32_t)(sb >> 32), tag);
+        }
+      }
+      for (int g = lane; g < a.world; g += 32) {
+        uint32_t d[4] = {0u, 0u, 0u, 0u};
+        per_mail_get(mine->stats[g], 4, tag, d, t.status);
+        s_stats[g][0] = __longlong_as_double((long long)(((unsigned long long)d[1] << 32) | d[0]));
+        s_stats[g][1] = __longlong_as_double((long long)(((unsigned long long)d[3] << 32) | d[2]));
+      }
+    }
+    __syncthreads();
+    stats = &s_stats[0][0];
+  }
+  if (!SHARDED && size <= 0) {  // host checks first; keep the device consistent anyway
     if (blockIdx.x == 0 && threadIdx.x == 0) per_flag(t.status, PER_EVT_EMPTY_BUFFER);
     return;
   }
@@ -406,6 +457,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       if (old == gridDim.x - 1) {  // last CTA: reset for the next launch, then release
         sc->mx_count = 0u;
         sc->mx_bits[(gen + 1u) & 1u] = 0u;
+        if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
         __threadfence();
         per_st_release(&sc->mx_gen, gen + 1u);
       }
@@ -419,9 +471,42 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
         __nanosleep(PER_SPIN_SLEEP_NS);
       }
       s_gmax = __uint_as_float(per_ld_relaxed_u32(&sc->mx_bits[gen & 1u]));
-      if (SHARDED && blockIdx.x == 0) *a.local_max = s_gmax;
+      if (a.use_rng && blockIdx.x == 0) *a.rng_counter = cbase + (unsigned long long)a.batch;
+      if (SHARDED) {  // every CTA has compacted its draws: the count is final
+        s_owned = per_ld_relaxed_u64(&sc->draws[gen & 1u]);
+        if (blockIdx.x == 0) {
+          *a.count = s_owned;
+          if (!a.p2p) *a.local_max = s_gmax;
+        }
+      }
     }
     __syncwarp();
+    if (SHARDED && a.p2p) {
+      // ---- max weight over all ranks: CTA 0 publishes this rank's max into
+      // every mailbox, every CTA reduces the slots of its own mailbox
+      const float lmax = s_gmax;
+      const unsigned long long seq = s_seq;
+      const uint32_t tag = per_mail_tag(seq);
+      PerMailbox* mine = a.mailboxes[a.rank];
+      if (blockIdx.x == 0) {
+        for (int g = lane; g < a.world; g += 32)
+          per_mail_put(&a.mailboxes[g]->max_w[a.rank], __float_as_uint(lmax), tag);
+      }
+      uint32_t mb = 0u;
+      for (int g = lane; g < a.world; g += 32) {
+        uint32_t d = 0u;
+        per_mail_get(&mine->max_w[g], 1, tag, &d, t.status);
+        mb = max(mb, d);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
+      if (lane == 0) {
+        s_gmax = __uint_as_float(mb);
+        // every CTA has read `seq` (all arrived at the grid exchange above)
+        if (blockIdx.x == 0) *(volatile unsigned long long*)&mine->seq = seq;
+      }
+      __syncwarp();
+    }
     named_bar_arrive(kBarGmaxReady, nthreads);
     return;
   }
@@ -436,24 +521,26 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     double S = 0.0, N = 0.0;
     for (int g = 0; g < a.world; ++g) {
       if (g == a.rank) base64 = S;
-      S += __ldg(a.stats + 2 * g);
-      N += __ldg(a.stats + 2 * g + 1);
+      S += stats[2 * g];
+      N += stats[2 * g + 1];
     }
     total64 = S;
     sizef = __double2float_rn(N);
+    if (!(N > 0.0) && blockIdx.x == 0 && threadIdx.x == 0) per_flag(t.status, PER_EVT_EMPTY_BUFFER);
   }
   const float total = __double2float_rn(total64);
   const float* leaves = t.levels[0];
   uint32_t n_fallback = 0, n_clamp = 0, n_zero = 0;
   uint32_t wmax_bits = 0u;
   float w_last = 0.f;  // this lane's unnormalised weight in its last tile
+  long long slot_last = -1;  // sharded: output slot of this lane's draw in its last tile
 
   for (; tile < a.num_tiles; tile += gridDim.x) {
     const bool last_tile = tile + gridDim.x >= a.num_tiles;
     const int64_t wj0 = tile * tile_draws + warp * 32;  // first draw of this warp
     const int64_t j = wj0 + lane;
     const bool ok = j < a.batch;
-    const float rnd = tile == blockIdx.x ? rnd0 : (ok ? __ldg(a.rand + j) : 0.f);
+    const float rnd = tile == blockIdx.x ? rnd0 : (ok ? draw_uniform(a, cbase, j) : 0.f);
 
     const float u = __fmul_rn(rnd, total);
     double r = (double)u;
@@ -466,16 +553,16 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       double S = 0.0;
       int owner = -1, lastpos = 0;
       for (int g = 0; g < a.world; ++g) {
-        const double tg = __ldg(a.stats + 2 * g);
+        const double tg = stats[2 * g];
         if (tg > 0.0) lastpos = g;
         S += tg;
         if (owner < 0 && S > r) owner = g;
       }
       if (owner < 0) owner = lastpos;
-      own = ok && owner == a.rank;
+      own = ok && owner == a.rank && size > 0;
       r -= base64;
       om = __ballot_sync(PER_FULL_MASK, own);
-      if (lane == 0 && om) obase = atomicAdd(a.count, (unsigned long long)__popc(om));
+      if (lane == 0 && om) obase = atomicAdd(&sc->draws[gen & 1u], (unsigned long long)__popc(om));
       obase = __shfl_sync(PER_FULL_MASK, obase, 0);
     }
 
@@ -563,6 +650,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
         a.w[slot] = wv;
         a.pos[slot] = (int32_t)j;
         s_rows[warp][orank] = (int32_t)i;
+        if (last_tile) {
+          slot_last = (long long)slot;
+          w_last = wv;
+        }
       }
       row0 = (int64_t)obase;
       nrows = __popc(om);
@@ -597,7 +688,15 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   // ---- normalise this warp's weights by the global max from the helper warp
   // (sharded: the caller normalises after reducing the max over the shards)
   named_bar_sync(kBarGmaxReady, nthreads);
-  if (SHARDED) return;
+  if (SHARDED) {
+    // in-kernel exchange (one tile per warp): normalise this lane's slot
+    if (a.p2p && slot_last >= 0) a.w[slot_last] = __fdiv_rn(w_last, s_gmax);
+    // entries past the owned draws read as padding (-1) for a following update
+    for (int64_t j = (int64_t)s_owned + (int64_t)blockIdx.x * tile_draws + warp * 32 + lane;
+         j < a.batch; j += (int64_t)gridDim.x * tile_draws)
+      a.idx[j] = -1;
+    return;
+  }
   const float gmax = s_gmax;
   for (int64_t tl = blockIdx.x; tl < a.num_tiles; tl += gridDim.x) {
     const int64_t j = tl * tile_draws + warp * 32 + lane;
@@ -609,7 +708,6 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
 template <int VEC, bool SHARDED>
 int launch_vec(SampleArgs a, cudaStream_t stream) {
   const void* fn = (const void*)per_sample_kernel<VEC, SHARDED>;
-  // compute warps per CTA: spread small batches one warp per SM, up to 8
   int sms = 148;
   {
     int dev = 0;
@@ -617,27 +715,62 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
   const int64_t warp_tiles = (a.batch + 31) / 32;
-  int64_t nw = (warp_tiles + sms - 1) / sms;
-  if (nw < 1) nw = 1;
-  if (nw > kMaxWarps) nw = kMaxWarps;
   // a few rows per SM: cp.async has the lower latency; many: bulk copies
   // keep more rows in flight
   if (a.use_bulk && warp_tiles <= sms) a.use_bulk = 0;
-  const int threads = (int)(nw + 1) * 32;
   const int n_top = (int)a.t.level_len[a.t.top_level];
   a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 15) & ~15;
-  const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
   int rc = per_set_smem(fn, (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes);
   if (rc) return rc;
+  // compute warps per CTA: among the shapes that cover the batch in one wave
+  // of co-resident CTAs (one tile per warp), the one whose busiest SM holds
+  // the fewest warps (CTAs are spread round-robin over the SMs); ties go to
+  // fewer, larger CTAs (fewer prologues). Batches beyond one wave: 8 warps.
+  int64_t nw = kMaxWarps, best_cost = -1;
   int max_ctas = 0;
-  rc = per_coresident_ctas(fn, threads, smem, &max_ctas);
-  if (rc) return rc;
+  for (int c = kMaxWarps; c >= 1; --c) {
+    int cap = 0;
+    rc = per_coresident_ctas(fn, (c + 1) * 32, (size_t)a.pre_bytes + (size_t)c * a.stage_bytes, &cap);
+    if (rc) return rc;
+    const int64_t tiles = (warp_tiles + c - 1) / c;
+    if (tiles > cap) continue;
+    const int64_t cost = (int64_t)c * ((tiles + sms - 1) / sms);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      nw = c;
+      max_ctas = cap;
+    }
+  }
+  const int threads = (int)(nw + 1) * 32;
+  const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
+  if (best_cost < 0) {
+    rc = per_coresident_ctas(fn, threads, smem, &max_ctas);
+    if (rc) return rc;
+  }
   a.num_tiles = (a.batch + nw * 32 - 1) / (nw * 32);
   int64_t grid = a.num_tiles < max_ctas ? a.num_tiles : max_ctas;
   if (grid < 1) grid = 1;
+  if (a.p2p && a.num_tiles > grid) return PER_ERR_TOO_LARGE;  // one tile per warp
   void* args[] = {&a};
   cudaError_t e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, grid > 1);
   return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+}
+
+// Largest batch that one wave of co-resident CTAs covers with one tile per
+// warp (the in-kernel exchange needs every CTA resident at once).
+template <int VEC>
+int max_wave_vec(SampleArgs a, int64_t* out) {
+  const void* fn = (const void*)per_sample_kernel<VEC, true>;
+  const int n_top = (int)a.t.level_len[a.t.top_level];
+  a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 15) & ~15;
+  const size_t smem = (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes;
+  int rc = per_set_smem(fn, smem);
+  if (rc) return rc;
+  int max_ctas = 0;
+  rc = per_coresident_ctas(fn, (kMaxWarps + 1) * 32, smem, &max_ctas);
+  if (rc) return rc;
+  *out = (int64_t)max_ctas * kMaxWarps * 32;
+  return PER_OK;
 }
 
 }  // namespace
@@ -663,6 +796,11 @@ void fill_common(SampleArgs& a, const PerTree& t, const float* rand, int64_t bat
   a.pos = nullptr;
   a.count = nullptr;
   a.local_max = nullptr;
+  a.mailboxes = nullptr;
+  a.p2p = 0;
+  a.use_rng = 0;
+  a.rng_seed = 0ull;
+  a.rng_counter = nullptr;
   // staged copies move whole pieces: 16 bytes when row starts and strides are
   // 16-byte aligned (rounding row_dim*4 up to 16 must stay inside the row
   // stride), else 8, else 4; bulk copies need the 16-byte case
@@ -707,15 +845,25 @@ int launch_any(SampleArgs& a, int vec, cudaStream_t stream) {
 
 }  // namespace
 
-int per_launch_sample(const PerTree& t, const float* rand, int64_t batch, float beta, float* out,
-                      int64_t out_stride, int64_t* idx, float* w, cudaStream_t stream) {
+void set_rng(SampleArgs& a, const PerRng* rng) {
+  if (!rng) return;
+  a.use_rng = 1;
+  a.rng_seed = rng->seed;
+  a.rng_counter = rng->counter;
+}
+
+int per_launch_sample(const PerTree& t, const float* rand, const PerRng* rng, int64_t batch,
+                      float beta, float* out, int64_t out_stride, int64_t* idx, float* w,
+                      cudaStream_t stream) {
   SampleArgs a;
   fill_common(a, t, rand, batch, beta, out, out_stride, idx, w);
+  set_rng(a, rng);
   return launch_any<false>(a, vec_width(t, out, out_stride), stream);
 }
 
 int per_launch_sample_sharded(const PerTree& t, int32_t rank, int32_t world, int64_t shard_base,
-                              const double* stats, const float* rand, int64_t batch, float beta,
+                              const double* stats, const float* rand, const PerRng* rng,
+                              int64_t batch, float beta,
                               float* out, int64_t out_stride, int64_t* idx, float* w,
                               int32_t* pos, int64_t* count, float* local_max,
                               cudaStream_t stream) {
@@ -728,8 +876,40 @@ int per_launch_sample_sharded(const PerTree& t, int32_t rank, int32_t world, int
   a.pos = pos;
   a.count = reinterpret_cast<unsigned long long*>(count);
   a.local_max = local_max;
-  cudaError_t e = cudaMemsetAsync(count, 0, sizeof(int64_t), stream);
-  if (e == cudaSuccess) e = cudaMemsetAsync(local_max, 0, sizeof(float), stream);
-  if (e != cudaSuccess) return per_record_cuda(e);
+  set_rng(a, rng);
+  // the kernel writes count, local_max and the -1 padding past the owned draws
   return launch_any<true>(a, vec_width(t, out, out_stride), stream);
+}
+
+int per_launch_sample_sharded_p2p(const PerTree& t, int32_t rank, int32_t world,
+                                  int64_t shard_base, PerMailbox* const* mailboxes,
+                                  const float* rand, const PerRng* rng, int64_t batch, float beta,
+                                  float* out, int64_t out_stride, int64_t* idx, float* w,
+                                  int32_t* pos, int64_t* count, cudaStream_t stream) {
+  SampleArgs a;
+  fill_common(a, t, rand, batch, beta, out, out_stride, idx, w);
+  a.rank = rank;
+  a.world = world;
+  a.shard_base = shard_base;
+  a.pos = pos;
+  a.count = reinterpret_cast<unsigned long long*>(count);
+  a.mailboxes = mailboxes;
+  a.p2p = 1;
+  set_rng(a, rng);
+  return launch_any<true>(a, vec_width(t, out, out_stride), stream);
+}
+
+int per_launch_sample_p2p_max_batch(const PerTree& t, int64_t* max_batch) {
+  SampleArgs a;
+  fill_common(a, t, nullptr, 1, 0.f, nullptr, t.row_dim, nullptr, nullptr);
+  int64_t best = INT64_MAX, m = 0;
+  int rc = max_wave_vec<4>(a, &m);
+  if (!rc) best = m < best ? m : best;
+  if (!rc) rc = max_wave_vec<2>(a, &m);
+  if (!rc) best = m < best ? m : best;
+  if (!rc) rc = max_wave_vec<1>(a, &m);
+  if (!rc) best = m < best ? m : best;
+  if (rc) return rc;
+  *max_batch = best;
+  return PER_OK;
 }

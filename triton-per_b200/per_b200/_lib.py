@@ -20,8 +20,10 @@ MAX_LEVELS = 7
 STATUS_WORDS = 16
 MAX_FIELDS = 16
 NOALLOC_MAX_CAPACITY = 1048576
+IPC_HANDLE_BYTES = 64
 
 i64 = ctypes.c_int64
+u64 = ctypes.c_uint64
 i32 = ctypes.c_int32
 vp = ctypes.c_void_p
 
@@ -96,6 +98,19 @@ SIGNATURES = {
     "per_sample_sharded": (ctypes.c_int, [ctypes.POINTER(Store), i32, i32, i64, vp, vp, i64,
                                           ctypes.c_float, vp, i64, vp, vp, vp, vp, vp, vp]),
     "per_normalize": (ctypes.c_int, [vp, vp, vp, i64, vp]),
+    "per_sample_fused_rng": (ctypes.c_int, [ctypes.POINTER(Store), u64, vp, i64, ctypes.c_float, vp,
+                                            i64, vp, vp, vp]),
+    "per_sample_sharded_rng": (ctypes.c_int, [ctypes.POINTER(Store), i32, i32, i64, vp, u64, vp, i64,
+                                              ctypes.c_float, vp, i64, vp, vp, vp, vp, vp, vp]),
+    "per_sample_sharded_p2p_rng": (ctypes.c_int, [ctypes.POINTER(Store), i32, i32, i64, vp, u64, vp,
+                                                  i64, ctypes.c_float, vp, i64, vp, vp, vp, vp, vp]),
+    "per_sample_sharded_p2p_max_batch": (ctypes.c_int, [ctypes.POINTER(Store), vp]),
+    "per_mailbox_create": (ctypes.c_int, [ctypes.POINTER(vp), vp]),
+    "per_mailbox_open": (ctypes.c_int, [vp, ctypes.POINTER(vp)]),
+    "per_mailbox_close": (ctypes.c_int, [vp]),
+    "per_mailbox_destroy": (ctypes.c_int, [vp]),
+    "per_sample_sharded_p2p": (ctypes.c_int, [ctypes.POINTER(Store), i32, i32, i64, vp, vp, i64,
+                                              ctypes.c_float, vp, i64, vp, vp, vp, vp, vp]),
     "per_update_priorities_shard": (ctypes.c_int, [ctypes.POINTER(Store), i64, vp, vp, i64, vp]),
     "per_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "per_last_cuda_error": (ctypes.c_int, []),
@@ -113,7 +128,7 @@ def header_functions(path: str = HEADER) -> list[str]:
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"per_b200: {LIB_PATH} is missing; build it with `python -m per_b200.build` "
+            f"per_b200: {LIB_PATH} is missing; build it with `python per_b200/build.py` "
             "(nvcc, sm_100a). There is no CPU fallback.")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():

@@ -90,6 +90,12 @@ class PERBuffer:
         self._max_priority = torch.ones((), device=dev)
         self._status = torch.zeros(_lib.STATUS_WORDS, dtype=torch.int32, device=dev)
         self._scratch = torch.zeros(int(lay.scratch_bytes), dtype=torch.uint8, device=dev)
+        # sample() draws its uniforms inside the kernel (Philox4x32-10, key
+        # rng_seed, position in this device word), where the reference calls
+        # torch.rand (buffer.py:85); the seed comes from torch's default
+        # generator, so torch.manual_seed() makes runs repeatable
+        self.rng_seed = int(torch.randint(0, 2**63 - 1, (1,)).item())
+        self._rng_counter = torch.zeros(1, dtype=torch.int64, device=dev)
 
         self.size = 0
         self._cursor = 0
@@ -145,8 +151,17 @@ class PERBuffer:
     def sample(self, batch_size: int, beta: float = 0.4):
         """Returns (fields: dict of views, indices, normalized IS weights)."""
         assert self.size > 0
-        rand = torch.rand(batch_size, device=self.device)
-        return self.sample_from_uniforms(rand, beta)
+        batch_size = int(batch_size)
+        out = torch.empty(batch_size, self.row_dim, device=self.device)
+        idx = torch.empty(batch_size, dtype=torch.int64, device=self.device)
+        w = torch.empty(batch_size, device=self.device)
+        with torch.cuda.device(self.device):
+            _lib.check("per_sample_fused_rng", _lib.lib.per_sample_fused_rng(
+                self._store_ref, self.rng_seed, self._rng_counter.data_ptr(), batch_size,
+                float(beta), out.data_ptr(), self.row_dim, idx.data_ptr(), w.data_ptr(),
+                _stream_ptr(self.device)))
+        views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
+        return views, idx, w
 
     def sample_from_uniforms(self, rand: torch.Tensor, beta: float = 0.4):
         """sample() with caller-provided uniforms in [0, 1) (float32, on the device)."""

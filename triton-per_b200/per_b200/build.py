@@ -1,6 +1,8 @@
 """Compile the engine's CUDA sources into the in-tree shared library.
 
-    python -m per_b200.build          # from triton-per_b200/
+    python per_b200/build.py          # from triton-per_b200/ (the package
+                                      # itself cannot be imported before the
+                                      # library exists)
 
 Produces per_b200/libper_b200.so for sm_100a (B200) only; the CUDA runtime is
 linked statically so the library loads on hosts without a driver (its entry

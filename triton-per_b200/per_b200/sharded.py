@@ -8,15 +8,25 @@ Rank g owns the global slots [g * C, (g + 1) * C) with C = ceil(capacity /
 world), in its own store on its own GPU; rows never leave their GPU.
 
 sample(batch_size, beta) is collective. Every rank draws the same
-`batch_size` global uniforms (a generator seeded identically on every rank),
-and the ranks exchange their shard totals and sizes (all-gather of 16 bytes
-per rank). A draw u = rand * total belongs to the shard whose range of the
-global priority prefix holds u: the union of the ranks' draws is exactly the
-draw of one buffer holding every slot, with IS weights (N * p / total)^-beta
-over the global size N and total. Each rank returns the draws it owns,
-compacted into the first `count` entries of full-size outputs (count is a
-device tensor; positions in the global batch are in `pos`); the weights are
-normalised by the max over all ranks (all-reduce of one float).
+`batch_size` global uniforms (a Philox stream drawn inside the sample
+kernel, with the same seed and position on every rank),
+and the ranks exchange their shard totals and sizes (16 bytes per rank). A
+draw u = rand * total belongs to the shard whose range of the global priority
+prefix holds u: the union of the ranks' draws is exactly the draw of one
+buffer holding every slot, with IS weights (N * p / total)^-beta over the
+global size N and total. Each rank returns the draws it owns, compacted into
+the first `count` entries of full-size outputs (count is a device tensor;
+positions in the global batch are in `pos`); the weights are normalised by
+the max over all ranks.
+
+The two exchanges run one of two ways:
+- peer memory (`exchange="p2p"`, the default when every rank has a GPU of
+  its own on one host): one kernel per sample; the statistics and the max
+  weight cross NVLink as system-scope stores into CUDA-IPC-mapped mailboxes,
+  waited on inside the kernel (bounded waits). Batches up to one wave of the
+  kernel (`p2p_max_batch`, ~75k draws on a B200);
+- collectives (`exchange="nccl"`, and larger batches): stats kernel,
+  all-gather, sample kernel, all-reduce MAX, normalise kernel.
 
 update_priorities(idx, td) applies the entries whose global index this rank
 owns (the data-parallel case: every rank updates the draws it sampled); with
@@ -30,6 +40,8 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
+import socket
 from typing import NamedTuple
 
 import torch
@@ -62,8 +74,9 @@ class CudaShard:
             _lib.check("per_shard_stats", _lib.lib.per_shard_stats(
                 self.buf._store_ref, out.data_ptr(), _stream_ptr(self.device)))
 
-    def sample(self, rank, world, base, all_stats, rand, beta):
-        b = rand.numel()
+    def sample(self, rank, world, base, all_stats, rand, beta, rng=None, batch=None):
+        """rand: global uniforms; or rng = (seed, device int64 counter) and `batch`."""
+        b = rand.numel() if rng is None else batch
         dev = self.device
         out = torch.empty(b, self.buf.row_dim, device=dev)
         idx = torch.empty(b, dtype=torch.int64, device=dev)
@@ -72,11 +85,48 @@ class CudaShard:
         count = torch.empty(1, dtype=torch.int64, device=dev)
         lmax = torch.empty(1, device=dev)
         with torch.cuda.device(dev):
-            _lib.check("per_sample_sharded", _lib.lib.per_sample_sharded(
-                self.buf._store_ref, rank, world, base, all_stats.data_ptr(), rand.data_ptr(), b,
-                float(beta), out.data_ptr(), self.buf.row_dim, idx.data_ptr(), w.data_ptr(),
-                pos.data_ptr(), count.data_ptr(), lmax.data_ptr(), _stream_ptr(dev)))
+            if rng is None:
+                _lib.check("per_sample_sharded", _lib.lib.per_sample_sharded(
+                    self.buf._store_ref, rank, world, base, all_stats.data_ptr(), rand.data_ptr(),
+                    b, float(beta), out.data_ptr(), self.buf.row_dim, idx.data_ptr(),
+                    w.data_ptr(), pos.data_ptr(), count.data_ptr(), lmax.data_ptr(),
+                    _stream_ptr(dev)))
+            else:
+                _lib.check("per_sample_sharded_rng", _lib.lib.per_sample_sharded_rng(
+                    self.buf._store_ref, rank, world, base, all_stats.data_ptr(), rng[0],
+                    rng[1].data_ptr(), b, float(beta), out.data_ptr(), self.buf.row_dim,
+                    idx.data_ptr(), w.data_ptr(), pos.data_ptr(), count.data_ptr(),
+                    lmax.data_ptr(), _stream_ptr(dev)))
         return out, idx, w, pos, count, lmax
+
+    def sample_p2p(self, rank, world, base, mailboxes, rand, beta, rng=None, batch=None):
+        b = rand.numel() if rng is None else batch
+        dev = self.device
+        out = torch.empty(b, self.buf.row_dim, device=dev)
+        idx = torch.empty(b, dtype=torch.int64, device=dev)
+        w = torch.empty(b, device=dev)
+        pos = torch.empty(b, dtype=torch.int32, device=dev)
+        count = torch.empty(1, dtype=torch.int64, device=dev)
+        with torch.cuda.device(dev):
+            if rng is None:
+                _lib.check("per_sample_sharded_p2p", _lib.lib.per_sample_sharded_p2p(
+                    self.buf._store_ref, rank, world, base, mailboxes.data_ptr(), rand.data_ptr(),
+                    b, float(beta), out.data_ptr(), self.buf.row_dim, idx.data_ptr(),
+                    w.data_ptr(), pos.data_ptr(), count.data_ptr(), _stream_ptr(dev)))
+            else:
+                _lib.check("per_sample_sharded_p2p_rng", _lib.lib.per_sample_sharded_p2p_rng(
+                    self.buf._store_ref, rank, world, base, mailboxes.data_ptr(), rng[0],
+                    rng[1].data_ptr(), b, float(beta), out.data_ptr(), self.buf.row_dim,
+                    idx.data_ptr(), w.data_ptr(), pos.data_ptr(), count.data_ptr(),
+                    _stream_ptr(dev)))
+        return out, idx, w, pos, count
+
+    def p2p_max_batch(self) -> int:
+        m = ctypes.c_int64(0)
+        with torch.cuda.device(self.device):
+            _lib.check("per_sample_sharded_p2p_max_batch",
+                       _lib.lib.per_sample_sharded_p2p_max_batch(self.buf._store_ref, ctypes.byref(m)))
+        return int(m.value)
 
     def normalize(self, w, count, gmax):
         with torch.cuda.device(self.device):
@@ -102,10 +152,14 @@ class ShardedPERBuffer:
         group=None,
         seed: int = 0,
         shard=None,
+        exchange: str = "auto",
     ):
+        if exchange not in ("auto", "p2p", "nccl"):
+            raise ValueError(f"exchange must be 'auto', 'p2p' or 'nccl', not {exchange!r}")
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        distributed = dist.is_available() and dist.is_initialized()
+        self.rank = dist.get_rank(group) if distributed else 0
+        self.world = dist.get_world_size(group) if distributed else 1
         self.capacity = capacity
         self.fields = dict(fields)
         self.alpha = alpha
@@ -121,11 +175,112 @@ class ShardedPERBuffer:
         for name, d in fields.items():
             self._offsets[name] = (o, o + d)
             o += d
-        # identical uniform streams on every rank
+        # identical uniform streams on every rank: the in-kernel Philox stream
+        # (seed, device counter) of the CUDA shard; a torch generator for
+        # other shard types
+        self.seed = int(seed) & 0xFFFFFFFFFFFFFFFF
         self._gen = torch.Generator(device=self.device).manual_seed(seed)
+        self._rng_counter = torch.zeros(1, dtype=torch.int64, device=self.device)
         self._stats = torch.zeros(2, dtype=torch.float64, device=self.device)
         self._all_flat = torch.zeros(self.world * 2, dtype=torch.float64, device=self.device)
         self._all_stats = self._all_flat.view(self.world, 2)
+        self._mailbox = None       # own mailbox (device pointer)
+        self._peer_boxes = []      # peers' mailboxes mapped into this process
+        self._mailboxes = None     # int64[world] device array of mailbox pointers
+        self.p2p_max_batch = 0
+        self.exchange = "nccl"
+        if exchange != "nccl" and isinstance(self.shard, CudaShard):
+            self._setup_p2p(required=exchange == "p2p")
+
+    # ------------------------------------------------------------ p2p set-up
+    def _p2p_possible(self) -> bool:
+        """Every rank on its own GPU of one host (the kernels wait on one another)."""
+        if self.world == 1:
+            return True
+        try:
+            gpu = str(torch.cuda.get_device_properties(self.device).uuid)
+        except (AttributeError, RuntimeError):
+            gpu = f"{os.environ.get('CUDA_VISIBLE_DEVICES', '')}:{self.device.index}"
+        me = (socket.gethostname(), gpu)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, me, group=self.group)
+        return len({h for h, _ in everyone}) == 1 and len({u for _, u in everyone}) == self.world
+
+    def _setup_p2p(self, required: bool) -> None:
+        if self.world > 1 and dist.get_backend(self.group) != "nccl":  # same on every rank
+            if required:
+                raise RuntimeError("exchange='p2p' needs the nccl backend")
+            return
+        ok = self._p2p_possible()
+        if ok:
+            box = ctypes.c_void_p()
+            handle = (ctypes.c_char * _lib.IPC_HANDLE_BYTES)()
+            with torch.cuda.device(self.device):
+                rc = _lib.lib.per_mailbox_create(ctypes.byref(box), handle)
+            ok = rc == 0
+            if ok:
+                self._mailbox = box.value
+        if self.world > 1:  # every rank takes the same path
+            flag = torch.tensor([1.0 if ok else 0.0], device=self.device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+            ok = flag.item() == 1.0
+        if ok:
+            handles = [bytes(handle)] * self.world
+            if self.world > 1:
+                dist.all_gather_object(handles, bytes(handle), group=self.group)
+            ptrs = []
+            opened = True
+            for g in range(self.world):
+                if g == self.rank:
+                    ptrs.append(self._mailbox)
+                    continue
+                p = ctypes.c_void_p()
+                with torch.cuda.device(self.device):
+                    rc = _lib.lib.per_mailbox_open(handles[g], ctypes.byref(p))
+                if rc:
+                    opened = False
+                    break
+                self._peer_boxes.append(p.value)
+                ptrs.append(p.value)
+            mb = self.shard.p2p_max_batch() if opened else 0
+            if self.world > 1:
+                t = torch.tensor([float(opened), float(mb)], device=self.device)
+                t_all = torch.empty(self.world * 2, device=self.device)
+                dist.all_gather_into_tensor(t_all, t, group=self.group)
+                t_all = t_all.view(self.world, 2)
+                opened = bool(t_all[:, 0].min().item() == 1.0)
+                mb = int(t_all[:, 1].min().item())
+            if opened:
+                self._mailboxes = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+                self.p2p_max_batch = mb
+                self.exchange = "p2p"
+                if self.world > 1:
+                    dist.barrier(group=self.group)
+                return
+            self._release_mailboxes()
+        if required:
+            raise RuntimeError("exchange='p2p' needs one GPU per rank on one host and CUDA IPC")
+
+    def _release_mailboxes(self) -> None:
+        with torch.cuda.device(self.device):
+            for p in self._peer_boxes:
+                _lib.lib.per_mailbox_close(ctypes.c_void_p(p))
+            self._peer_boxes = []
+            if self._mailbox is not None:
+                _lib.lib.per_mailbox_destroy(ctypes.c_void_p(self._mailbox))
+                self._mailbox = None
+        self._mailboxes = None
+        self.p2p_max_batch = 0
+        self.exchange = "nccl"
+
+    def close(self) -> None:
+        """Collective: unmap and free the mailboxes (peer-memory exchange)."""
+        if self._mailbox is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no peer still writes into our mailbox
+        self._release_mailboxes()
 
     # ------------------------------------------------------------------ add
     def add(self, batch: dict[str, torch.Tensor]) -> None:
@@ -135,17 +290,36 @@ class ShardedPERBuffer:
     # --------------------------------------------------------------- sample
     def sample(self, batch_size: int, beta: float = 0.4) -> ShardSample:
         """Collective: this rank's share of a global batch of `batch_size` draws."""
-        rand = torch.rand(batch_size, generator=self._gen, device=self.device)
-        return self.sample_from_uniforms(rand, beta)
+        if not isinstance(self.shard, CudaShard):
+            rand = torch.rand(batch_size, generator=self._gen, device=self.device)
+            return self.sample_from_uniforms(rand, beta)
+        rng = (self.seed, self._rng_counter)
+        if self.exchange == "p2p" and batch_size <= self.p2p_max_batch:
+            out, idx, w, pos, count = self.shard.sample_p2p(
+                self.rank, self.world, self.base, self._mailboxes, None, beta, rng, batch_size)
+        else:
+            self._exchange_stats()
+            out, idx, w, pos, count, lmax = self.shard.sample(
+                self.rank, self.world, self.base, self._all_stats, None, beta, rng, batch_size)
+            if self.world > 1:
+                dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
+            self.shard.normalize(w, count, lmax)
+        views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
+        return ShardSample(views, idx, w, count, pos)
 
     def sample_from_uniforms(self, rand: torch.Tensor, beta: float = 0.4) -> ShardSample:
         """sample() with caller-provided global uniforms (identical on every rank)."""
         rand = rand.to(device=self.device, dtype=torch.float32).contiguous()
-        self.shard.stats(self._stats)
-        dist.all_gather_into_tensor(self._all_flat, self._stats, group=self.group)
+        if self.exchange == "p2p" and rand.numel() <= self.p2p_max_batch:
+            out, idx, w, pos, count = self.shard.sample_p2p(
+                self.rank, self.world, self.base, self._mailboxes, rand, beta)
+            views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
+            return ShardSample(views, idx, w, count, pos)
+        self._exchange_stats()
         out, idx, w, pos, count, lmax = self.shard.sample(
             self.rank, self.world, self.base, self._all_stats, rand, beta)
-        dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
+        if self.world > 1:
+            dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
         self.shard.normalize(w, count, lmax)
         views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
         return ShardSample(views, idx, w, count, pos)
@@ -169,8 +343,14 @@ class ShardedPERBuffer:
             idx, td = all_idx, all_td
         self.shard.update(self.base, idx, td)
 
+    def _exchange_stats(self) -> None:
+        if self.world > 1:
+            self.shard.stats(self._stats)
+            dist.all_gather_into_tensor(self._all_flat, self._stats, group=self.group)
+        else:
+            self.shard.stats(self._all_flat)
+
     def global_stats(self) -> torch.Tensor:
         """[world, 2] (total priority, live size) of every shard (collective)."""
-        self.shard.stats(self._stats)
-        dist.all_gather_into_tensor(self._all_flat, self._stats, group=self.group)
+        self._exchange_stats()
         return self._all_stats.clone()
