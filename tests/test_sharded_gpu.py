@@ -162,3 +162,41 @@ def test_single_rank_p2p_exchange_equals_single_buffer():
     st = sb.shard.buf.status()
     assert st["errors"] == 0 and st["timeouts"] == 0
     sb.close()
+
+
+def test_peer_that_never_publishes_times_out_with_a_status_flag():
+    """The in-kernel exchange against a peer mailbox that nothing ever writes
+    (a zeroed device buffer standing in for rank 1): every wait gives up after
+    its time limit (about a second), the kernel flags PER_EVT_PEER_TIMEOUT and
+    counts the timeouts, returns, and the context stays usable."""
+    rng = np.random.default_rng(23)
+    cap = 50_000
+    buf = make_buffer(cap, {"x": 3}, {"x": rng.standard_normal((cap, 3), dtype=np.float32)},
+                      rng.lognormal(0.0, 1.0, cap).astype(np.float32))
+    mine = ctypes.c_void_p()
+    handle = (ctypes.c_char * _lib.IPC_HANDLE_BYTES)()
+    assert _lib.lib.per_mailbox_create(ctypes.byref(mine), handle) == 0
+    silent = torch.zeros(4096, dtype=torch.uint8, device="cuda")  # never written
+    boxes = torch.tensor([mine.value, silent.data_ptr()], dtype=torch.int64, device="cuda")
+    b = 64
+    rand = torch.rand(b, device="cuda")
+    out = torch.empty(b, 3, device="cuda")
+    idx = torch.empty(b, dtype=torch.int64, device="cuda")
+    w = torch.empty(b, device="cuda")
+    pos = torch.empty(b, dtype=torch.int32, device="cuda")
+    count = torch.empty(1, dtype=torch.int64, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = _lib.lib.per_sample_sharded_p2p(buf._store_ref, 0, 2, 0, boxes.data_ptr(), rand.data_ptr(),
+                                         b, 0.4, out.data_ptr(), 3, idx.data_ptr(), w.data_ptr(),
+                                         pos.data_ptr(), count.data_ptr(), stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    st = buf.status()
+    assert st["errors"] & 0x10, st  # PER_EVT_PEER_TIMEOUT
+    assert st["timeouts"] >= 2, st   # the statistics wait and the max wait
+    # the context is still usable: an ordinary sample afterwards
+    buf.clear_status()
+    views, i2, w2 = buf.sample(256, 0.4)
+    torch.cuda.synchronize()
+    assert buf.status()["errors"] == 0 and (i2 >= 0).all()
+    assert _lib.lib.per_mailbox_destroy(mine) == 0

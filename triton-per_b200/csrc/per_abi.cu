@@ -34,6 +34,18 @@ bool cooperative_enabled() {
   return v == 1;
 }
 
+// Launches carry a programmatic dependency on the previous kernel of the
+// stream (the kernel may start early and waits with griddepcontrol.wait),
+// except cooperative launches; PER_PDL=0 turns it off.
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("PER_PDL");
+    v = (s && s[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 PerTree tree_of(const per_store_t* s) {
   PerTree t;
   for (int k = 0; k < PER_MAX_LEVELS; ++k) {
@@ -158,10 +170,15 @@ cudaError_t per_launch(const void* fn, unsigned grid, unsigned threads, size_t s
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  if (coop) {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = coop ? 1 : 0;
+  cfg.numAttrs = (coop || pdl_enabled()) ? 1 : 0;
   cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

@@ -103,6 +103,15 @@ __device__ __forceinline__ void per_flag(uint32_t* status, uint32_t bit) {
   if (status) atomicOr(status + PER_STATUS_ERRORS, bit);
 }
 
+// Programmatic dependent launch: kernels are launched so that they may start
+// while the previous kernel on the stream is still running. Each kernel waits
+// here, before it reads anything an earlier kernel wrote (no-op when the
+// launch had no programmatic dependency), then lets the next kernel launch.
+__device__ __forceinline__ void per_wait_previous_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ unsigned long long per_globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

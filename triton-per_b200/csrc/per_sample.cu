@@ -331,6 +331,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     per_mbar_init(&s_mbar[warp], 1);
     per_fence_mbar_init();
   }
+  per_wait_previous_grid();
 
   // early, independent loads: generation of the max exchange, size, first uniform
   const uint32_t gen = SHARDED || (helper && lane == 0) ? per_ld_relaxed_u32(&sc->mx_gen) : 0u;
@@ -419,12 +420,13 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     __syncthreads();
     const uint32_t tag = per_mail_tag(s_seq);
     if (warp == 0) {
+      const double tot = s_pre[ppos(n_top)];
+      const double szd = (double)size;
       if (blockIdx.x == 0) {
-        const double tot = s_pre[ppos(n_top)];
-        const double szd = (double)size;
         const unsigned long long tb = (unsigned long long)__double_as_longlong(tot);
         const unsigned long long sb = (unsigned long long)__double_as_longlong(szd);
         for (int g = lane; g < a.world; g += 32) {
+          if (g == a.rank) continue;  // every CTA of this rank has its own values
           unsigned long long* slot = a.mailboxes[g]->stats[a.rank];
           per_mail_put(slot + 0, (uint32_t)tb, tag);
           per_mail_put(slot + 1, (uint32_t)(tb >> 32), tag);
@@ -433,6 +435,11 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
         }
       }
       for (int g = lane; g < a.world; g += 32) {
+        if (g == a.rank) {
+          s_stats[g][0] = tot;
+          s_stats[g][1] = szd;
+          continue;
+        }
         uint32_t d[4] = {0u, 0u, 0u, 0u};
         per_mail_get(mine->stats[g], 4, tag, d, t.status);
         s_stats[g][0] = __longlong_as_double((long long)(((unsigned long long)d[1] << 32) | d[0]));
@@ -490,10 +497,11 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       PerMailbox* mine = a.mailboxes[a.rank];
       if (blockIdx.x == 0) {
         for (int g = lane; g < a.world; g += 32)
-          per_mail_put(&a.mailboxes[g]->max_w[a.rank], __float_as_uint(lmax), tag);
+          if (g != a.rank) per_mail_put(&a.mailboxes[g]->max_w[a.rank], __float_as_uint(lmax), tag);
       }
-      uint32_t mb = 0u;
+      uint32_t mb = __float_as_uint(lmax);
       for (int g = lane; g < a.world; g += 32) {
+        if (g == a.rank) continue;
         uint32_t d = 0u;
         per_mail_get(&mine->max_w[g], 1, tag, &d, t.status);
         mb = max(mb, d);

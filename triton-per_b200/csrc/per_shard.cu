@@ -21,6 +21,7 @@ constexpr int kThreads = 256;
 // out[0] = total priority of the store (float64 sum of its top-level nodes),
 // out[1] = live size.
 __global__ void __launch_bounds__(kThreads) per_shard_stats_kernel(PerTree t, double* out) {
+  per_wait_previous_grid();
   __shared__ double s_part[kThreads / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* topv = t.levels[t.top_level];
@@ -42,6 +43,7 @@ __global__ void __launch_bounds__(kThreads) per_shard_stats_kernel(PerTree t, do
 
 __global__ void per_normalize_kernel(float* w, const int64_t* count, const float* gmax,
                                      int64_t cap) {
+  per_wait_previous_grid();
   const int64_t n = min(*count, cap);
   const float m = *gmax;
   for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n;

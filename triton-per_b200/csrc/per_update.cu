@@ -55,6 +55,7 @@ __device__ __forceinline__ float new_priority(const PerTree& t, float td) {
 
 // ---------------------------------------------------------------- grid update
 __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
+  per_wait_previous_grid();
   const PerTree& t = a.t;
   PerGridBarrier bar;
   bar.init(t.scratch);
@@ -165,6 +166,7 @@ __device__ __forceinline__ int hset_insert(uint32_t* keys, uint32_t key) {
 }
 
 __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a) {
+  per_wait_previous_grid();
   const PerTree& t = a.t;
   extern __shared__ __align__(16) unsigned char s_dyn[];  // per-warp node tiles
   __shared__ uint32_t s_wkey[kHash];    // slot -> leaf index
@@ -288,6 +290,7 @@ struct AddArgs {
 };
 
 __global__ void __launch_bounds__(kThreads) per_add_kernel(AddArgs a) {
+  per_wait_previous_grid();
   const PerTree& t = a.t;
   __shared__ __align__(16) unsigned char s_tiles[kThreads / 32][PER_NODE_TILE];
   PerGridBarrier bar;
@@ -344,6 +347,7 @@ __global__ void __launch_bounds__(kThreads) per_add_kernel(AddArgs a) {
 
 // ---------------------------------------------------------------- rebuild
 __global__ void __launch_bounds__(kThreads) per_rebuild_kernel(PerTree t) {
+  per_wait_previous_grid();
   __shared__ __align__(16) unsigned char s_tiles[kThreads / 32][PER_NODE_TILE];
   PerGridBarrier bar;
   bar.init(t.scratch);
