@@ -23,12 +23,13 @@
 struct PerScratch {
   uint32_t bar_count;    // arrivals at the current grid barrier
   uint32_t bar_gen;      // generation, bumped by the last arriver
-  uint32_t mx_count;     // sample: warps that published their max weight
-  uint32_t mx_gen;       // sample: generation, bumped when every warp has published
-  uint32_t mx_bits[2];   // sample: running max weight bits, by generation parity
+  uint32_t mx_count;     // sample, large grids: CTAs that published their max weight
+  uint32_t mx_gen;       // sample: launch generation, bumped once every CTA has published
+  uint32_t mx_bits[2];   // sample, large grids: running max weight bits, by generation parity
   unsigned long long draws[2];  // sharded sample: owned-draw counter, by generation parity
-  uint32_t pad[54];      // keep partial[] 256-byte aligned
-  float partial[PER_MAX_GRID];
+  uint32_t pad[54];      // keep mx_slot[] 256-byte aligned
+  // sample, small grids: per CTA (generation + 1) << 32 | CTA max weight bits
+  unsigned long long mx_slot[PER_MAX_GRID / 2];
 };
 static_assert(sizeof(PerScratch) == PER_SCRATCH_BYTES, "scratch layout");
 
@@ -64,6 +65,16 @@ __device__ __forceinline__ unsigned long long per_ld_relaxed_sys_u64(const unsig
 
 __device__ __forceinline__ void per_mail_put(unsigned long long* p, uint32_t data, uint32_t tag) {
   per_st_relaxed_sys_u64(p, ((unsigned long long)tag << 32) | data);
+}
+
+__device__ __forceinline__ void per_st_release_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long per_ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ uint32_t per_ld_acquire(const uint32_t* p) {

@@ -87,17 +87,6 @@ __device__ __forceinline__ float draw_uniform(const SampleArgs& a, unsigned long
 // Padded position of prefix entry i: one spare double every 32.
 __device__ __forceinline__ int ppos(int i) { return i + (i >> 5); }
 
-// Number of k in [1, n] with pre[k] <= t, i.e. the first node whose inclusive
-// prefix exceeds t (n if none). Branch-free binary lifting, per lane.
-__device__ __forceinline__ int upper_bound_pre(const double* pre, int n, double t) {
-  int pos = 0;
-  for (int step = 1 << (31 - __clz(n)); step > 0; step >>= 1) {
-    const int np = pos + step;
-    pos = (np <= n && pre[ppos(np)] <= t) ? np : pos;
-  }
-  return pos;
-}
-
 // Number of k in [1, n] with pre[k] < t: the first node whose inclusive prefix
 // reaches t (n if none).
 __device__ __forceinline__ int lower_bound_pre(const double* pre, int n, double t) {
@@ -105,6 +94,46 @@ __device__ __forceinline__ int lower_bound_pre(const double* pre, int n, double 
   for (int step = 1 << (31 - __clz(n)); step > 0; step >>= 1) {
     const int np = pos + step;
     pos = (np <= n && pre[ppos(np)] < t) ? np : pos;
+  }
+  return pos;
+}
+
+// Number of k in [1, n] with pre[k] <= t, t given as its float64 bits: the
+// top-level node holding t (n if t is at or past the total). Integer
+// compares: non-negative float64 values order like their bit patterns, and a
+// negative t (a draw owned by another shard) compares below every prefix, as
+// in float64. Two forms:
+//  - n <= 1024 (at most 32 groups of 32 nodes): lane l holds the prefix at
+//    the end of group l (`grp`, bits; INT64_MAX past the last group); five
+//    shuffle steps find the group, five shared-memory steps the node in it;
+//  - larger n: a branch-free binary search over all n + 1 entries.
+__device__ __forceinline__ int upper_bound_top(const double* pre, int n, long long tb,
+                                               long long grp) {
+  if (n <= 32 * 32) {
+    const int G = n >> 5;
+    int m = 0;
+#pragma unroll
+    for (int step = 16; step > 0; step >>= 1) {
+      const int nm = m + step;
+      const long long v = __shfl_sync(PER_FULL_MASK, grp, nm - 1);
+      m = (nm <= G && v <= tb) ? nm : m;
+    }
+    if (m >= G) return n;
+    int pos = m << 5;
+#pragma unroll
+    for (int step = 16; step > 0; step >>= 1) {
+      const int np = pos + step;
+      pos = __double_as_longlong(pre[ppos(np)]) <= tb ? np : pos;
+    }
+    return pos;
+  }
+  int pos = 0;
+#pragma unroll
+  for (int step = PER_TOP_MAX; step > 0; step >>= 1) {
+    const int np = pos + step;
+    const bool in = np <= n;
+    const long long v = __double_as_longlong(pre[ppos(in ? np : 0)]);
+    pos = (in && v <= tb) ? np : pos;
   }
   return pos;
 }
@@ -301,6 +330,8 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 // Named barriers between the compute warps and the CTA's helper warp.
 constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
 constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
+constexpr int kMaxGrid = PER_MAX_GRID;  // CTAs of one launch (scratch sized for it)
+constexpr int kAllToAllCtas = 32;  // max exchange: every CTA reads every slot up to this grid
 
 template <int VEC, bool SHARDED>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(SampleArgs a) {
@@ -334,7 +365,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   per_wait_previous_grid();
 
   // early, independent loads: generation of the max exchange, size, first uniform
-  const uint32_t gen = SHARDED || (helper && lane == 0) ? per_ld_relaxed_u32(&sc->mx_gen) : 0u;
+  const uint32_t gen = SHARDED || helper ? per_ld_relaxed_u32(&sc->mx_gen) : 0u;
   const int64_t size = __ldg(t.size_cursor);
   // every CTA reads the stream position before it arrives at the max exchange;
   // CTA 0 advances it after the exchange has completed
@@ -458,26 +489,60 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     // ---- helper warp: exchange the batch max with the other CTAs while the
     // compute warps gather their rows
     named_bar_sync(kBarMaxReady, nthreads);
-    if (lane == 0) {
+    uint32_t mb = 0u;
+    bool timed_out = false;
+    if (gridDim.x <= kAllToAllCtas) {
+      // small grids: every CTA publishes its max in its own slot, tagged with
+      // this launch's generation, and every helper reads all slots
+      const uint32_t tag = gen + 1u;
+      if (lane == 0)
+        per_st_release_u64(&sc->mx_slot[blockIdx.x], ((unsigned long long)tag << 32) | s_cta_max);
+      if (lane < (int)gridDim.x) {
+        unsigned long long v = per_ld_acquire_u64(&sc->mx_slot[lane]);
+        for (uint32_t it = 0; (uint32_t)(v >> 32) != tag; ++it) {
+          if (it > PER_SPIN_LIMIT) {
+            timed_out = true;
+            break;
+          }
+          __nanosleep(PER_SPIN_SLEEP_NS);
+          v = per_ld_acquire_u64(&sc->mx_slot[lane]);
+        }
+        mb = (uint32_t)v;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
+      if (lane == 0 && blockIdx.x == 0) {  // all CTAs have read gen: next generation
+        sc->mx_bits[(gen + 1u) & 1u] = 0u;
+        if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
+        sc->mx_gen = gen + 1u;
+      }
+    } else if (lane == 0) {
+      // large grids: one running max and an arrival counter; the last CTA
+      // resets the other parity's words and releases the next generation
       atomicMax(&sc->mx_bits[gen & 1u], s_cta_max);
       const uint32_t old = per_atom_add_acq_rel(&sc->mx_count, 1u);
-      if (old == gridDim.x - 1) {  // last CTA: reset for the next launch, then release
+      if (old == gridDim.x - 1) {
         sc->mx_count = 0u;
         sc->mx_bits[(gen + 1u) & 1u] = 0u;
         if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
         __threadfence();
         per_st_release(&sc->mx_gen, gen + 1u);
       }
-      uint32_t it = 0;
-      while (per_ld_acquire(&sc->mx_gen) == gen) {
-        if (++it > PER_SPIN_LIMIT) {
-          per_flag(t.status, PER_EVT_BARRIER_TIMEOUT);
-          per_count(t.status, PER_STATUS_TIMEOUTS);
+      for (uint32_t it = 0; per_ld_acquire(&sc->mx_gen) == gen; ++it) {
+        if (it > PER_SPIN_LIMIT) {
+          timed_out = true;
           break;
         }
         __nanosleep(PER_SPIN_SLEEP_NS);
       }
-      s_gmax = __uint_as_float(per_ld_relaxed_u32(&sc->mx_bits[gen & 1u]));
+      mb = per_ld_relaxed_u32(&sc->mx_bits[gen & 1u]);
+    }
+    if (__any_sync(PER_FULL_MASK, timed_out) && lane == 0) {
+      per_flag(t.status, PER_EVT_BARRIER_TIMEOUT);
+      per_count(t.status, PER_STATUS_TIMEOUTS);
+    }
+    if (lane == 0) {
+      s_gmax = __uint_as_float(mb);
       if (a.use_rng && blockIdx.x == 0) *a.rng_counter = cbase + (unsigned long long)a.batch;
       if (SHARDED) {  // every CTA has compacted its draws: the count is final
         s_owned = per_ld_relaxed_u64(&sc->draws[gen & 1u]);
@@ -493,23 +558,23 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       // every mailbox, every CTA reduces the slots of its own mailbox
       const float lmax = s_gmax;
       const unsigned long long seq = s_seq;
-      const uint32_t tag = per_mail_tag(seq);
+      const uint32_t mtag = per_mail_tag(seq);
       PerMailbox* mine = a.mailboxes[a.rank];
       if (blockIdx.x == 0) {
         for (int g = lane; g < a.world; g += 32)
-          if (g != a.rank) per_mail_put(&a.mailboxes[g]->max_w[a.rank], __float_as_uint(lmax), tag);
+          if (g != a.rank) per_mail_put(&a.mailboxes[g]->max_w[a.rank], __float_as_uint(lmax), mtag);
       }
-      uint32_t mb = __float_as_uint(lmax);
+      uint32_t gb = __float_as_uint(lmax);
       for (int g = lane; g < a.world; g += 32) {
         if (g == a.rank) continue;
         uint32_t d = 0u;
-        per_mail_get(&mine->max_w[g], 1, tag, &d, t.status);
-        mb = max(mb, d);
+        per_mail_get(&mine->max_w[g], 1, mtag, &d, t.status);
+        gb = max(gb, d);
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
+      for (int o = 16; o > 0; o >>= 1) gb = max(gb, __shfl_xor_sync(PER_FULL_MASK, gb, o));
       if (lane == 0) {
-        s_gmax = __uint_as_float(mb);
+        s_gmax = __uint_as_float(gb);
         // every CTA has read `seq` (all arrived at the grid exchange above)
         if (blockIdx.x == 0) *(volatile unsigned long long*)&mine->seq = seq;
       }
@@ -538,6 +603,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   }
   const float total = __double2float_rn(total64);
   const float* leaves = t.levels[0];
+  // end of top-level group `lane` (32 nodes per group), for upper_bound_top
+  const long long grp = 32 * (lane + 1) <= n_top
+                            ? __double_as_longlong(s_pre[ppos(32 * (lane + 1))])
+                            : 0x7fffffffffffffffll;
   uint32_t n_fallback = 0, n_clamp = 0, n_zero = 0;
   uint32_t wmax_bits = 0u;
   float w_last = 0.f;  // this lane's unnormalised weight in its last tile
@@ -576,7 +645,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
 
     // top level: binary search of the staged prefix
     bool fb = false;
-    int k = upper_bound_pre(s_pre, n_top, r);
+    int k = upper_bound_top(s_pre, n_top, __double_as_longlong(r), grp);
     if (k >= n_top) {  // at or past the store's total: last node with mass
       k = lower_bound_pre(s_pre, n_top, ltotal64);
       if (k >= n_top) k = n_top - 1;
@@ -608,7 +677,6 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     }
 
     int64_t i = node;
-    float wv = 0.f;
     if (own) {
       if (i > size - 1 || ltotal64 <= 0.0) {  // sampling.py:49-51 clamp; p reloaded there
         i = size - 1;
@@ -635,6 +703,29 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
         ++n_zero;
       }
       n_fallback += fb ? 1u : 0u;
+    }
+
+    // rows of this warp's draws: the first copies go out now and land while
+    // the weights are computed
+    int64_t row0;  // first output row of this warp's gathered rows
+    int nrows;
+    int orank = 0;
+    if (SHARDED) {  // compact the owned draws into [obase, obase + popc(om))
+      orank = __popc(om & ((1u << lane) - 1u));
+      if (own) s_rows[warp][orank] = (int32_t)i;
+      row0 = (int64_t)obase;
+      nrows = __popc(om);
+    } else {
+      s_rows[warp][lane] = (int32_t)i;
+      row0 = wj0;
+      nrows = (int)min((int64_t)32, a.batch - wj0);
+    }
+    __syncwarp();
+    const int rps = a.rows_per_stage;
+    if (rps > 0 && nrows > 0) gather_issue(a, stage, s_rows[warp], 0, min(rps, nrows), lane, &s_mbar[warp]);
+
+    float wv = 0.f;
+    if (own) {
       const float prob = __fdiv_rn(p, total);
       wv = powf(__fmul_rn(sizef, prob), -a.beta);
       wmax_bits = max(wmax_bits, __float_as_uint(wv));
@@ -648,39 +739,27 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       __syncwarp();
       named_bar_arrive(kBarMaxReady, nthreads);
     }
-    int64_t row0;  // first output row of this warp's gathered rows
-    int nrows;
-    if (SHARDED) {  // compact the owned draws into [obase, obase + popc(om))
-      const int orank = __popc(om & ((1u << lane) - 1u));
+    if (SHARDED) {
       if (own) {
         const unsigned long long slot = obase + orank;
         a.idx[slot] = a.shard_base + i;
         a.w[slot] = wv;
         a.pos[slot] = (int32_t)j;
-        s_rows[warp][orank] = (int32_t)i;
         if (last_tile) {
           slot_last = (long long)slot;
           w_last = wv;
         }
       }
-      row0 = (int64_t)obase;
-      nrows = __popc(om);
-    } else {
-      if (ok) {
-        a.idx[j] = i;
-        if (!last_tile) a.w[j] = wv;
-      }
-      s_rows[warp][lane] = (int32_t)i;
-      row0 = wj0;
-      nrows = (int)min((int64_t)32, a.batch - wj0);
+    } else if (ok) {
+      a.idx[j] = i;
+      if (!last_tile) a.w[j] = wv;
     }
-    __syncwarp();
 
-    // ---- gather this warp's rows
-    if (a.rows_per_stage > 0) {
-      for (int r0 = 0; r0 < nrows; r0 += a.rows_per_stage) {
-        const int rn = min(a.rows_per_stage, nrows - r0);
-        gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp]);
+    // ---- finish the gather of this warp's rows
+    if (rps > 0) {
+      for (int r0 = 0; r0 < nrows; r0 += rps) {
+        const int rn = min(rps, nrows - r0);
+        if (r0 > 0) gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp]);
         gather_finish<VEC>(a, stage, row0 + r0, rn, lane, &s_mbar[warp], phase);
       }
     } else if (nrows > 0) {
@@ -741,7 +820,7 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     rc = per_coresident_ctas(fn, (c + 1) * 32, (size_t)a.pre_bytes + (size_t)c * a.stage_bytes, &cap);
     if (rc) return rc;
     const int64_t tiles = (warp_tiles + c - 1) / c;
-    if (tiles > cap) continue;
+    if (tiles > cap || tiles > kMaxGrid) continue;
     const int64_t cost = (int64_t)c * ((tiles + sms - 1) / sms);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
@@ -757,6 +836,7 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
   }
   a.num_tiles = (a.batch + nw * 32 - 1) / (nw * 32);
   int64_t grid = a.num_tiles < max_ctas ? a.num_tiles : max_ctas;
+  if (grid > kMaxGrid) grid = kMaxGrid;
   if (grid < 1) grid = 1;
   if (a.p2p && a.num_tiles > grid) return PER_ERR_TOO_LARGE;  // one tile per warp
   void* args[] = {&a};
@@ -777,6 +857,7 @@ int max_wave_vec(SampleArgs a, int64_t* out) {
   int max_ctas = 0;
   rc = per_coresident_ctas(fn, (kMaxWarps + 1) * 32, smem, &max_ctas);
   if (rc) return rc;
+  if (max_ctas > kMaxGrid) max_ctas = kMaxGrid;
   *out = (int64_t)max_ctas * kMaxWarps * 32;
   return PER_OK;
 }
