@@ -96,6 +96,10 @@ class PERBuffer:
         # generator, so torch.manual_seed() makes runs repeatable
         self.rng_seed = int(torch.randint(0, 2**63 - 1, (1,)).item())
         self._rng_counter = torch.zeros(1, dtype=torch.int64, device=dev)
+        self._rng_counter_ptr = self._rng_counter.data_ptr()
+        self._dev_index = self.device.index
+        self._names = tuple(self._offsets)
+        self._dims = tuple(b - a for a, b in self._offsets.values())
 
         self.size = 0
         self._cursor = 0
@@ -151,48 +155,58 @@ class PERBuffer:
     def sample(self, batch_size: int, beta: float = 0.4):
         """Returns (fields: dict of views, indices, normalized IS weights)."""
         assert self.size > 0
-        batch_size = int(batch_size)
-        out = torch.empty(batch_size, self.row_dim, device=self.device)
-        idx = torch.empty(batch_size, dtype=torch.int64, device=self.device)
-        w = torch.empty(batch_size, device=self.device)
-        with torch.cuda.device(self.device):
-            _lib.check("per_sample_fused_rng", _lib.lib.per_sample_fused_rng(
-                self._store_ref, self.rng_seed, self._rng_counter.data_ptr(), batch_size,
-                float(beta), out.data_ptr(), self.row_dim, idx.data_ptr(), w.data_ptr(),
-                _stream_ptr(self.device)))
-        views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
-        return views, idx, w
+        b = int(batch_size)
+        out, idx, w = self._outputs(b)
+        self._call("per_sample_fused_rng", _lib.lib.per_sample_fused_rng, self._store_ref,
+                   self.rng_seed, self._rng_counter_ptr, b, float(beta), out.data_ptr(),
+                   self.row_dim, idx.data_ptr(), w.data_ptr())
+        return dict(zip(self._names, out.split(self._dims, dim=1))), idx, w
 
     def sample_from_uniforms(self, rand: torch.Tensor, beta: float = 0.4):
         """sample() with caller-provided uniforms in [0, 1) (float32, on the device)."""
         assert self.size > 0
         if rand.dtype != torch.float32 or rand.device != self.device or not rand.is_contiguous():
             rand = rand.to(device=self.device, dtype=torch.float32).contiguous()
-        batch_size = rand.numel()
-        out = torch.empty(batch_size, self.row_dim, device=self.device)
-        idx = torch.empty(batch_size, dtype=torch.int64, device=self.device)
-        w = torch.empty(batch_size, device=self.device)
-        with torch.cuda.device(self.device):
-            _lib.check("per_sample_fused", _lib.lib.per_sample_fused(
-                self._store_ref, rand.data_ptr(), batch_size, float(beta), out.data_ptr(),
-                self.row_dim, idx.data_ptr(), w.data_ptr(), _stream_ptr(self.device)))
-        views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
-        return views, idx, w
+        b = rand.numel()
+        out, idx, w = self._outputs(b)
+        self._call("per_sample_fused", _lib.lib.per_sample_fused, self._store_ref,
+                   rand.data_ptr(), b, float(beta), out.data_ptr(), self.row_dim,
+                   idx.data_ptr(), w.data_ptr())
+        return dict(zip(self._names, out.split(self._dims, dim=1))), idx, w
+
+    def _outputs(self, b: int):
+        """Fresh [b, row_dim] rows and [b] weights (one float32 allocation), [b] indices."""
+        flat = torch.empty(b * (self.row_dim + 1), device=self.device)
+        n = b * self.row_dim
+        return (flat[:n].view(b, self.row_dim), torch.empty(b, dtype=torch.int64, device=self.device),
+                flat[n:])
+
+    def _call(self, name, fn, *args) -> None:
+        """fn(*args, stream) on this buffer's device and current stream; raises on error."""
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if torch.cuda.current_device() != self._dev_index:
+            with torch.cuda.device(self.device):
+                rc = fn(*args, stream)
+        else:
+            rc = fn(*args, stream)
+        if rc:
+            _lib.check(name, rc)
 
     # --------------------------------------------------------------- update
     def update_priorities(self, indices: torch.Tensor, td_errors: torch.Tensor) -> None:
-        td = td_errors.detach().reshape(-1)
+        td = td_errors.detach() if td_errors.requires_grad else td_errors
+        if td.dim() != 1:
+            td = td.reshape(-1)
         if td.dtype != torch.float32 or td.device != self.device or not td.is_contiguous():
             td = td.to(device=self.device, dtype=torch.float32).contiguous()
-        idx = indices.reshape(-1)
+        idx = indices if indices.dim() == 1 else indices.reshape(-1)
         if idx.dtype != torch.int64 or idx.device != self.device or not idx.is_contiguous():
             idx = idx.to(device=self.device, dtype=torch.int64).contiguous()
-        if idx.numel() != td.numel():
-            raise ValueError(f"{idx.numel()} indices but {td.numel()} TD errors")
-        with torch.cuda.device(self.device):
-            _lib.check("per_update_priorities", _lib.lib.per_update_priorities(
-                self._store_ref, idx.data_ptr(), td.data_ptr(), idx.numel(),
-                _stream_ptr(self.device)))
+        n = idx.numel()
+        if n != td.numel():
+            raise ValueError(f"{n} indices but {td.numel()} TD errors")
+        self._call("per_update_priorities", _lib.lib.per_update_priorities, self._store_ref,
+                   idx.data_ptr(), td.data_ptr(), n)
 
     # ------------------------------------------------------------ utilities
     def rebuild_sums(self) -> None:
