@@ -272,6 +272,24 @@ def make_store(device, seed, priorities="absnormal"):
     return buf
 
 
+def make_wide_store(device, seed=11, capacity=2_000_000, row_dim=4096):
+    """2M x 4096 float32 rows ~U(0,1) (32 GB, image-feature-like), priorities
+    (|N(0,1)| + 1e-6)^0.6: the wide-row gather configuration."""
+    from per_b200 import PERBuffer
+
+    buf = PERBuffer(capacity, {"feat": row_dim}, device=device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    chunk = 100_000
+    for s0 in range(0, capacity, chunk):
+        n = min(chunk, capacity - s0)
+        buf.add({"feat": torch.rand(n, row_dim, generator=g, device=device)})
+    leaves = (torch.randn(capacity, generator=g, device=device).abs() + 1e-6) ** 0.6
+    buf.priorities[:capacity] = leaves
+    buf.rebuild_sums()
+    torch.cuda.synchronize()
+    return buf
+
+
 def utd_step(buf, row, td):
     """One step of the high-UTD loop: add 1, then 32 x (sample 256 -> update 256)."""
     buf.add(row)
@@ -319,14 +337,14 @@ def time_replays(g, iters, world):
     return a.elapsed_time(b)  # ms
 
 
-def kernel_time_us(buf, batch, reps=20, launches=16, seed=7):
+def kernel_time_us(buf, batch, reps=20, launches=16, seed=7, beta=BETA):
     """Average CUDA-event time of one fused-sample launch (graph of `launches`)."""
     g0 = torch.Generator(device=buf.device).manual_seed(seed)
     rands = [torch.rand(batch, generator=g0, device=buf.device) for _ in range(launches)]
 
     def fn():
         for r in rands:
-            buf.sample_from_uniforms(r, BETA)
+            buf.sample_from_uniforms(r, beta)
 
     g = capture(fn, warm=2)
     for _ in range(3):
@@ -736,6 +754,15 @@ def main():
         storm = update_time_us(heavy, 65536, reps=5, launches=4)
         sweep.append({"update_storm_65536_us": round(storm, 2)})
         del heavy
+        torch.cuda.empty_cache()
+        # wide rows: 2M x 4096 (32 GB), batch 1024, beta 0.6 (sample kernel +
+        # whole-GPU row gather kernel per call)
+        wide = make_wide_store(dev)
+        wus = kernel_time_us(wide, 1024, reps=10, launches=8, beta=0.6)
+        wgbs = algo_bytes(1024, 4096) / (wus * 1e-6) / 1e9
+        sweep.append({"wide_rows_2Mx4096_batch1024_us": round(wus, 3), "gbs": round(wgbs, 1),
+                      "frac": round(wgbs / peak, 4), "samples_per_s": round(1024 / (wus * 1e-6))})
+        del wide
         torch.cuda.empty_cache()
 
     e2e = None

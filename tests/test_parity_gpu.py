@@ -161,7 +161,8 @@ def test_wide_rows_gather_bit_exact():
     assert r["equal"] + r["excused"] == 1024
 
 
-@pytest.mark.parametrize("row_dim", [1, 2, 3, 4, 5, 8, 64, 74, 127, 128, 129, 300, 522])
+@pytest.mark.parametrize("row_dim", [1, 2, 3, 4, 5, 8, 64, 74, 127, 128, 129, 300, 522,
+                                     2560, 2561, 2562, 4099])
 def test_gather_every_vector_width(row_dim):
     rng = np.random.default_rng(row_dim)
     cap = 3000

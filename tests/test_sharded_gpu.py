@@ -52,14 +52,17 @@ def _sample_all(shards, rand, beta):
     return res
 
 
-@pytest.mark.parametrize("world,shard_cap,full", [(3, 40_000, True), (4, 5_000, False),
-                                                  (2, 300_000, True)])
-def test_union_of_shards_equals_one_buffer(world, shard_cap, full):
+@pytest.mark.parametrize("world,shard_cap,full,wide", [(3, 40_000, True, False),
+                                                       (4, 5_000, False, False),
+                                                       (2, 300_000, True, False),
+                                                       (2, 3_000, False, True)])
+def test_union_of_shards_equals_one_buffer(world, shard_cap, full, wide):
     rng = np.random.default_rng(world * 7 + shard_cap)
     total = world * shard_cap
-    fields = {"a": 5, "b": 3}
-    rows = {"a": rng.standard_normal((total, 5), dtype=np.float32),
-            "b": rng.standard_normal((total, 3), dtype=np.float32)}
+    da, db = (2600, 3) if wide else (5, 3)  # wide: rows copied by the separate gather kernel
+    fields = {"a": da, "b": db}
+    rows = {"a": rng.standard_normal((total, da), dtype=np.float32),
+            "b": rng.standard_normal((total, db), dtype=np.float32)}
     leaves = rng.lognormal(0.0, 1.5, total).astype(np.float32)
     sizes = [shard_cap] * world
     if not full:  # partially filled last shard, and one shard without any mass

@@ -289,36 +289,6 @@ __device__ __forceinline__ void gather_finish(const SampleArgs& a, unsigned char
   __syncwarp();
 }
 
-// Wide rows: each row copied directly by the whole warp, 8 vectors per lane in flight.
-template <int VEC>
-__device__ __forceinline__ void gather_direct(const SampleArgs& a, const int32_t* s_idx,
-                                              int64_t j0, int nrows, int lane) {
-  using V = typename VecT<VEC>::T;
-  const int nvec = a.nvec;
-  const V* src = reinterpret_cast<const V*>(a.t.storage);
-  V* dst = reinterpret_cast<V*>(a.out);
-  const int64_t sstride = a.t.row_stride / VEC;
-  const int64_t dstride = a.out_stride / VEC;
-  constexpr int U = 8;
-  for (int r = 0; r < nrows; ++r) {
-    const V* s = src + (int64_t)s_idx[r] * sstride;
-    V* d = dst + (j0 + r) * dstride;
-    for (int c0 = 0; c0 < nvec; c0 += 32 * U) {
-      V buf[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int c = c0 + u * 32 + lane;
-        if (c < nvec) buf[u] = __ldcs(s + c);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int c = c0 + u * 32 + lane;
-        if (c < nvec) d[c] = buf[u];
-      }
-    }
-  }
-}
-
 __device__ __forceinline__ void named_bar_arrive(int id, int count) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
@@ -762,9 +732,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
         if (r0 > 0) gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp]);
         gather_finish<VEC>(a, stage, row0 + r0, rn, lane, &s_mbar[warp], phase);
       }
-    } else if (nrows > 0) {
-      gather_direct<VEC>(a, s_rows[warp], row0, nrows, lane);
-    }
+    }  // rows wider than a stage: copied by per_gather_rows_kernel after this kernel
   }
 
   if (lane == 0) {
@@ -924,12 +892,87 @@ int vec_width(const PerTree& t, const float* out, int64_t out_stride) {
   return (al % 16 == 0 && t.row_dim % 4 == 0) ? 4 : (al % 8 == 0 && t.row_dim % 2 == 0) ? 2 : 1;
 }
 
+// ---- rows wider than a warp's staging tile (row_dim > 2560): the sample
+// kernel writes the indices only, then this kernel copies the rows with the
+// whole GPU: one row per CTA per step, every thread keeping 4 vectors in
+// flight, streaming loads and stores (the rows are read once).
+struct GatherArgs {
+  const float* storage;
+  int64_t row_stride;
+  int64_t row_dim;
+  float* out;
+  int64_t out_stride;
+  const int64_t* idx;
+  int64_t base;                    // idx are global slot numbers (sharded): slot = idx - base
+  const unsigned long long* count; // rows to copy on the device (sharded), or null
+  int64_t batch;
+};
+constexpr int kGatherThreads = 256;
+constexpr int kGatherUnroll = 4;
+
+template <int VEC>
+__global__ void __launch_bounds__(kGatherThreads) per_gather_rows_kernel(GatherArgs g) {
+  per_wait_previous_grid();
+  using V = typename VecT<VEC>::T;
+  int64_t n = g.batch;
+  if (g.count) n = min(n, (int64_t)*g.count);
+  const int nvec = (int)(g.row_dim / VEC);
+  for (int64_t j = blockIdx.x; j < n; j += gridDim.x) {
+    const int64_t slot = g.idx[j] - g.base;
+    const V* src = reinterpret_cast<const V*>(g.storage + slot * g.row_stride);
+    V* dst = reinterpret_cast<V*>(g.out + j * g.out_stride);
+    for (int c0 = 0; c0 < nvec; c0 += kGatherThreads * kGatherUnroll) {
+      V buf[kGatherUnroll];
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u) {
+        const int c = c0 + u * kGatherThreads + threadIdx.x;
+        if (c < nvec) buf[u] = __ldcs(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < kGatherUnroll; ++u) {
+        const int c = c0 + u * kGatherThreads + threadIdx.x;
+        if (c < nvec) __stcs(dst + c, buf[u]);
+      }
+    }
+  }
+}
+
+int launch_gather_rows(const SampleArgs& a, int vec, int64_t base, cudaStream_t stream) {
+  GatherArgs g;
+  g.storage = a.t.storage;
+  g.row_stride = a.t.row_stride;
+  g.row_dim = a.t.row_dim;
+  g.out = a.out;
+  g.out_stride = a.out_stride;
+  g.idx = a.idx;
+  g.base = base;
+  g.count = a.count;
+  g.batch = a.batch;
+  const void* fn = vec == 4   ? (const void*)per_gather_rows_kernel<4>
+                   : vec == 2 ? (const void*)per_gather_rows_kernel<2>
+                              : (const void*)per_gather_rows_kernel<1>;
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  int64_t grid = (int64_t)sms * 8;  // 8 CTAs (2048 threads) per SM
+  if (grid > a.batch) grid = a.batch;
+  if (grid < 1) grid = 1;
+  void* args[] = {&g};
+  cudaError_t e = per_launch(fn, (unsigned)grid, kGatherThreads, 0, stream, args, false);
+  return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+}
+
 template <bool SHARDED>
 int launch_any(SampleArgs& a, int vec, cudaStream_t stream) {
   a.nvec = (int32_t)(a.t.row_dim / vec);
-  if (vec == 4) return launch_vec<4, SHARDED>(a, stream);
-  if (vec == 2) return launch_vec<2, SHARDED>(a, stream);
-  return launch_vec<1, SHARDED>(a, stream);
+  int rc = vec == 4   ? launch_vec<4, SHARDED>(a, stream)
+           : vec == 2 ? launch_vec<2, SHARDED>(a, stream)
+                      : launch_vec<1, SHARDED>(a, stream);
+  if (rc || a.rows_per_stage > 0) return rc;
+  return launch_gather_rows(a, vec, SHARDED ? a.shard_base : 0, stream);
 }
 
 }  // namespace

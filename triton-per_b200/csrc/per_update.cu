@@ -281,6 +281,216 @@ __global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a
   }
 }
 
+// ---------------------------------------------------------------- prefetched update
+// Batches of up to kLMaxN indices whose lines fit in shared memory. The nodes
+// that an update touches are known from the leaf indices alone (node of level
+// L = leaf >> 5L), so every 32-child line the recompute needs (children of
+// every touched node of every level) is fetched at once, right after the
+// election: one L2 round trip for the whole update instead of one per level.
+// The new values are then patched into the staged lines (winning leaves
+// first, then each recomputed node into its parent's line) and every level
+// is summed from shared memory. Node values are the same per_sum32_tree of
+// the same children as in the other update paths, so the tree bits do not
+// depend on the path.
+constexpr int kLPer = 2;                   // entries per thread
+constexpr int kLMaxN = kThreads * kLPer;   // 512
+constexpr int kLHashBits = 10;
+constexpr int kLHash = 1 << kLHashBits;    // load factor <= 1/2
+constexpr int kLMaxT = 4;                  // tree levels above the leaves
+constexpr size_t kLinesSmemMax = 200 * 1024;  // shared memory the kernel may ask for
+
+__device__ __forceinline__ uint32_t lslot(uint32_t key) {
+  return (key * 2654435761u) >> (32 - kLHashBits);
+}
+
+__device__ __forceinline__ int lset_insert(uint32_t* keys, uint32_t key) {
+  uint32_t s = lslot(key);
+  for (int probe = 0; probe < kLHash; ++probe) {
+    const uint32_t prev = atomicCAS(&keys[s], kEmpty, key);
+    if (prev == kEmpty || prev == key) return (int)s;
+    s = (s + 1) & (kLHash - 1);
+  }
+  return -1;
+}
+
+// Shared-memory bytes of the prefetched update for T levels above the leaves
+// and up to ncap nodes per level.
+__host__ __device__ __forceinline__ size_t lines_smem(int T, int ncap) {
+  return (size_t)T * ncap * PER_LINE_STRIDE          // staged lines
+         + (size_t)(2 + 2 * T) * kLHash * 4          // election table, node sets + positions
+         + (size_t)2 * T * ncap * 4;                 // node lists + parents' set slots
+}
+
+__global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a, int ncap) {
+  const PerTree& t = a.t;
+  const int T = t.num_levels - 1;
+  extern __shared__ __align__(16) unsigned char s_dyn[];
+  unsigned char* lines = s_dyn;            // [T][ncap] staged lines
+  uint32_t* wkey = reinterpret_cast<uint32_t*>(lines + (size_t)T * ncap * PER_LINE_STRIDE);
+  uint32_t* wval = wkey + kLHash;
+  uint32_t* skey = wval + kLHash;          // [T][kLHash] node sets
+  uint32_t* spos = skey + T * kLHash;      // [T][kLHash] list position of each set slot
+  uint32_t* list = spos + T * kLHash;      // [T][ncap] touched nodes per level
+  uint32_t* pslot = list + T * ncap;       // [T][ncap] set slot of the node's parent
+  __shared__ int s_cnt[kLMaxT];
+  __shared__ uint32_t s_max;
+  __shared__ uint32_t s_fresh[kThreads / 32][32];  // list positions of a warp's new nodes
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lbase = per_smem_addr_generic(lines);
+
+  // tables are cleared while the previous kernel may still run
+  for (int k = threadIdx.x; k < kLHash; k += kThreads) {
+    wkey[k] = kEmpty;
+    wval[k] = 0u;
+    for (int L = 0; L < T; ++L) skey[L * kLHash + k] = kEmpty;
+  }
+  if (threadIdx.x < kLMaxT) s_cnt[threadIdx.x] = 0;
+  if (threadIdx.x == 0) s_max = 0u;
+  per_wait_previous_grid();
+  int64_t li[kLPer];
+  float tdv[kLPer];
+#pragma unroll
+  for (int q = 0; q < kLPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    li[q] = e < a.n ? slot_of(a, e) : -1;
+    tdv[q] = e < a.n ? a.td[e] : 0.f;
+  }
+  __syncthreads();
+
+  // election (the last occurrence of a slot wins: largest position). Every
+  // valid entry also enters the node of each level above its leaf; the entry
+  // that adds a node first gives it a list position and fetches its line
+  // right away (the winner of a slot touches the same nodes)
+  int slot[kLPer], lslot0[kLPer];
+  float np[kLPer];
+  uint32_t tmax = 0u, nbad = 0u, nforeign = 0u;
+#pragma unroll
+  for (int q = 0; q < kLPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    slot[q] = -1;
+    lslot0[q] = -1;
+    np[q] = 0.f;
+    bool valid = false;
+    if (e < a.n) {
+      if (li[q] < 0 || li[q] >= t.capacity) {
+        if (a.strict) ++nbad; else ++nforeign;
+      } else {
+        valid = true;
+        np[q] = new_priority(t, tdv[q]);
+        tmax = max(tmax, __float_as_uint(np[q]));
+        slot[q] = lset_insert(wkey, (uint32_t)li[q]);
+        if (slot[q] >= 0) atomicMax(&wval[slot[q]], (uint32_t)(e + 1));
+      }
+    }
+    uint32_t nd = valid ? (uint32_t)li[q] >> PER_LOG_FANOUT : 0u;
+    int below_p = -1;  // list position of the node entered at the level below, if new
+    for (int L = 0; L < T; ++L) {
+      int sl = -1;
+      bool fresh = false;
+      if (valid) {
+        uint32_t h = lslot(nd);
+        uint32_t* keys = skey + L * kLHash;
+        for (int probe = 0; probe < kLHash; ++probe) {
+          const uint32_t prev = atomicCAS(&keys[h], kEmpty, nd);
+          if (prev == kEmpty || prev == nd) {
+            sl = (int)h;
+            fresh = prev == kEmpty;
+            break;
+          }
+          h = (h + 1) & (kLHash - 1);
+        }
+      }
+      // list positions for the warp's new nodes: one shared counter add
+      const uint32_t m = __ballot_sync(PER_FULL_MASK, fresh);
+      int pbase = 0;
+      if (lane == 0 && m) pbase = atomicAdd(&s_cnt[L], __popc(m));
+      pbase = __shfl_sync(PER_FULL_MASK, pbase, 0);
+      const int newp = fresh ? pbase + __popc(m & ((1u << lane) - 1u)) : -1;
+      if (L == 0) lslot0[q] = sl;
+      if (below_p >= 0) pslot[(L - 1) * ncap + below_p] = (uint32_t)sl;  // parent of that node
+      const int nf = __popc(m);
+      if (fresh) {
+        list[L * ncap + newp] = nd;
+        spos[L * kLHash + sl] = (uint32_t)newp;
+        s_fresh[warp][newp - pbase] = (uint32_t)newp;
+      }
+      __syncwarp();
+      // the warp fetches its new nodes' lines together, 4 lines (8 x 16 B
+      // each) per instruction
+      const float* clevel = t.levels[L];
+      for (int g = lane >> 3; g < nf; g += 4) {
+        const int p = (int)s_fresh[warp][g];
+        const int part = lane & 7;
+        per_cp_async16(lbase + (uint32_t)((L * ncap + p) * PER_LINE_STRIDE + part * 16),
+                       clevel + (int64_t)list[L * ncap + p] * PER_FANOUT + part * 4);
+      }
+      __syncwarp();
+      below_p = newp;
+      nd >>= PER_LOG_FANOUT;
+    }
+  }
+  if (nbad) {
+    per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
+    per_flag(t.status, PER_EVT_BAD_INDEX);
+  }
+  if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
+  if (lane == 0 && tmax) atomicMax(&s_max, tmax);
+  __syncthreads();
+  if (threadIdx.x == 0 && s_max) atomicMax(reinterpret_cast<unsigned int*>(t.max_priority), s_max);
+
+  // winners write their leaf; every thread waits for the lines it fetched
+  bool win[kLPer];
+#pragma unroll
+  for (int q = 0; q < kLPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    win[q] = slot[q] >= 0 && wval[slot[q]] == (uint32_t)(e + 1);
+    if (win[q]) t.levels[0][li[q]] = np[q];
+  }
+  per_cp_async_wait_all();
+  __syncthreads();
+
+  // the winning leaves go into their chunk lines
+#pragma unroll
+  for (int q = 0; q < kLPer; ++q) {
+    if (win[q]) {
+      float* line = reinterpret_cast<float*>(lines + (size_t)spos[lslot0[q]] * PER_LINE_STRIDE);
+      line[li[q] & (PER_FANOUT - 1)] = np[q];
+    }
+  }
+  __syncthreads();
+
+  // level by level: sum each touched node's line, store it, patch it into
+  // its parent's line
+  for (int L = 0; L < T; ++L) {
+    for (int p = threadIdx.x; p < s_cnt[L]; p += kThreads) {
+      const uint32_t node = list[L * ncap + p];
+      const float4* row =
+          reinterpret_cast<const float4*>(lines + (size_t)(L * ncap + p) * PER_LINE_STRIDE);
+      float c[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = row[i];
+        c[4 * i] = v.x;
+        c[4 * i + 1] = v.y;
+        c[4 * i + 2] = v.z;
+        c[4 * i + 3] = v.w;
+      }
+      const float v = per_sum32_tree(c);
+      t.levels[L + 1][node] = v;
+      if (L + 1 < T) {
+        const uint32_t pp = spos[(L + 1) * kLHash + pslot[L * ncap + p]];
+        float* pline = reinterpret_cast<float*>(
+            lines + (size_t)((L + 1) * ncap + pp) * PER_LINE_STRIDE);
+        pline[node & (PER_FANOUT - 1)] = v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------- add
 struct AddArgs {
   PerTree t;
@@ -398,6 +608,19 @@ int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, cons
   a.n = n;
   a.base = base;
   a.strict = strict;
+  const int T = t.num_levels - 1;
+  const int ncap = (int)((n + 31) / 32 * 32);
+  if (n <= kLMaxN && T <= kLMaxT && lines_smem(T, ncap) <= kLinesSmemMax) {
+    const void* fl = (const void*)per_update_lines_kernel;
+    const size_t smem = lines_smem(T, ncap);
+    int rc = per_set_smem(fl, lines_smem(kLMaxT, kLMaxN) < kLinesSmemMax ? lines_smem(kLMaxT, kLMaxN)
+                                                                         : kLinesSmemMax);
+    if (rc) return rc;
+    int nc = ncap;
+    void* args[] = {&a, &nc};
+    cudaError_t e = per_launch(fl, 1, kThreads, smem, stream, args, false);
+    return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+  }
   if (n <= kSmallMax) {
     const void* fs = (const void*)per_update_small_kernel;
     int rc = per_set_smem(fs, kSmallDynSmem);
