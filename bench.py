@@ -328,10 +328,12 @@ def time_replays(g, iters, world):
     b = torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("timed")  # the launch list (ncu --nvtx-include timed/)
     a.record(st)
     for _ in range(iters):
         g.replay()
     b.record(st)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     return a.elapsed_time(b)  # ms
@@ -630,12 +632,12 @@ def cpu_loop(seconds=None, steps=None, warmup=0, threads=None):
 
 
 # ---------------------------------------------------------------- main
-def traffic_from_profiles():
-    """dram bytes per launch of the fused sample at batch 256, from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "sample_kernel_1Mx74.md")
+def traffic_from_profiles(key="traffic_bytes_per_launch_b256", name="sample_kernel_1Mx74.md"):
+    """dram bytes per launch from a committed ncu summary (one ncu capture)."""
+    p = os.path.join(ROOT, "profiles", name)
     try:
         for line in open(p):
-            if line.startswith("traffic_bytes_per_launch_b256:"):
+            if line.startswith(key + ":"):
                 return int(float(line.split(":", 1)[1]))
     except OSError:
         pass
@@ -678,17 +680,21 @@ def main():
     ap.add_argument("--kernel-only", type=int, default=0, metavar="BATCH",
                     help="profiling aid: eager fused samples of this batch (then updates of 256) "
                          "on the 1M x 74 store, no timing output")
+    ap.add_argument("--wide-rows", type=int, default=0, metavar="CAPACITY",
+                    help="with --kernel-only: a CAPACITY x 4096 store of the wide-row "
+                         "configuration instead (profiling aid; the bench uses 2M rows)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     if args.kernel_only:
         dev = torch.device("cuda", 0)
         torch.cuda.set_device(dev)
-        buf = make_store(dev, seed=1)
+        buf = make_wide_store(dev, capacity=args.wide_rows) if args.wide_rows else make_store(dev, seed=1)
+        beta = 0.6 if args.wide_rows else BETA
         g = torch.Generator(device=dev).manual_seed(2)
         for _ in range(args.warmup + args.steps):
             r = torch.rand(args.kernel_only, generator=g, device=dev)
-            _, idx, _ = buf.sample_from_uniforms(r, BETA)
+            _, idx, _ = buf.sample_from_uniforms(r, beta)
             buf.update_priorities(idx[:BATCH], torch.rand(min(BATCH, idx.numel()), device=dev))
         torch.cuda.synchronize()
         st = buf.status()
@@ -738,7 +744,15 @@ def main():
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic_from_profiles(),
                 "peak_source": peak_kind, "kernel": "per_sample_kernel",
-                "kernel_us": k_us, "algo_bytes_per_launch": ab}
+                "kernel_us": k_us, "algo_bytes_per_launch": ab, "batch": BATCH}
+    # the same kernel at the large-batch end of the sweep (1M x 74, batch 65,536)
+    k64 = kernel_time_us(buf, 65536, reps=10, launches=8)
+    ab64 = algo_bytes(65536, ROW_DIM)
+    a64 = ab64 / (k64 * 1e-6) / 1e9
+    roofline_large = {"bound": "hbm", "achieved": a64, "peak": peak, "unit": "GB/s",
+                      "frac": a64 / peak, "peak_source": peak_kind, "kernel": "per_sample_kernel",
+                      "traffic": traffic_from_profiles("traffic_bytes_per_launch_b65536"),
+                      "kernel_us": k64, "algo_bytes_per_launch": ab64, "batch": 65536}
 
     sweep = None
     if not args.no_sweep and rank == 0:
@@ -789,7 +803,7 @@ def main():
                        "l2": "storage 296 MB > 126 MB L2 (tree 4 MB stays resident)",
                        "timing": "CUDA graph of one step, CUDA events, max over ranks"},
             "update_us": u_us,
-            "roofline": roofline,
+            "roofline": roofline, "roofline_batch65536": roofline_large,
             "sweep": sweep,
             "e2e": e2e,
             "cpu_baseline": cpu,
