@@ -280,6 +280,14 @@ int per_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap
 int per_update_priorities_shard(const per_store_t* store, int64_t base, const int64_t* idx,
                                 const float* td, int64_t n, void* stream);
 
+/* per_update_priorities_shard() applied to the first min(n, *count) entries
+ * only (`count` is a device int64, e.g. the count written by a sharded
+ * sample, whose idx array is padded with -1 past it): the host sizes the
+ * launch for n without reading the device count. */
+int per_update_priorities_shard_count(const per_store_t* store, int64_t base, const int64_t* idx,
+                                      const float* td, int64_t n, const int64_t* count,
+                                      void* stream);
+
 /* Human-readable name of a PER_* return code. */
 const char* per_error_string(int code);
 

@@ -65,7 +65,10 @@ class CpuShard:
         n = int(count.item())
         w[:n] = w[:n] / gmax
 
-    def update(self, base, idx, td):
+    def update(self, base, idx, td, count=None):
+        if count is not None:  # only the owned prefix of a sharded sample's idx
+            n = int(count.item())
+            idx, td = idx[:n], td[:n]
         i = idx.numpy() - base
         keep = (i >= 0) & (i < self.capacity)
         if keep.any():

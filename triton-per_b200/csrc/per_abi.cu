@@ -453,7 +453,20 @@ int per_update_priorities_shard(const per_store_t* store, int64_t base, const in
   if (base < 0) return PER_ERR_INVALID_ARGUMENT;
   if (n < 1) return PER_ERR_EMPTY;
   if (n >= (int64_t)0xffffffffLL) return PER_ERR_TOO_LARGE;
-  return per_launch_update_shard(tree_of(store), base, 0, idx, td, n, (cudaStream_t)stream);
+  return per_launch_update_shard(tree_of(store), base, 0, idx, td, n, nullptr, (cudaStream_t)stream);
+}
+
+int per_update_priorities_shard_count(const per_store_t* store, int64_t base, const int64_t* idx,
+                                      const float* td, int64_t n, const int64_t* count,
+                                      void* stream) {
+  int rc = check_store(store);
+  if (rc) return rc;
+  if (!idx || !td || !count) return PER_ERR_NULL_POINTER;
+  if (base < 0) return PER_ERR_INVALID_ARGUMENT;
+  if (n < 1) return PER_ERR_EMPTY;
+  if (n >= (int64_t)0xffffffffLL) return PER_ERR_TOO_LARGE;
+  if (((uintptr_t)count) % 8) return PER_ERR_MISALIGNED;
+  return per_launch_update_shard(tree_of(store), base, 0, idx, td, n, count, (cudaStream_t)stream);
 }
 
 int per_rebuild_sums(const per_store_t* store, void* stream) {

@@ -41,7 +41,7 @@ int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int
 // Update with global indices: slot = idx - base; indices outside the store
 // are errors when strict, else skipped and counted as another shard's.
 int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, const int64_t* idx,
-                            const float* td, int64_t n, cudaStream_t stream);
+                            const float* td, int64_t n, const int64_t* count, cudaStream_t stream);
 int per_launch_sample_sharded(const PerTree& t, int32_t rank, int32_t world, int64_t shard_base,
                               const double* stats, const float* rand, const PerRng* rng,
                               int64_t batch, float beta, float* out, int64_t out_stride,

@@ -609,8 +609,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       own = ok && owner == a.rank && size > 0;
       r -= base64;
       om = __ballot_sync(PER_FULL_MASK, own);
+      // lane 0 reserves the warp's output slots; the result is broadcast only
+      // after the search, so the atomic's round trip overlaps it
       if (lane == 0 && om) obase = atomicAdd(&sc->draws[gen & 1u], (unsigned long long)__popc(om));
-      obase = __shfl_sync(PER_FULL_MASK, obase, 0);
     }
 
     // top level: binary search of the staged prefix
@@ -681,6 +682,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     int nrows;
     int orank = 0;
     if (SHARDED) {  // compact the owned draws into [obase, obase + popc(om))
+      obase = __shfl_sync(PER_FULL_MASK, obase, 0);
       orank = __popc(om & ((1u << lane) - 1u));
       if (own) s_rows[warp][orank] = (int32_t)i;
       row0 = (int64_t)obase;

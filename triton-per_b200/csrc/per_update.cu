@@ -42,7 +42,14 @@ struct UpdateArgs {
   int64_t n;
   int64_t base;    // global index of slot 0 (sharded stores); 0 otherwise
   int32_t strict;  // 1: indices outside the store are errors; 0: another shard's (skipped)
+  const unsigned long long* count;  // device: entries to apply (a prefix of idx), or null = n
 };
+
+// Entries to apply: all n, or the device count when one is given (read after
+// the previous kernel's results are visible).
+__device__ __forceinline__ int64_t entries_of(const UpdateArgs& a) {
+  return a.count ? min(a.n, (int64_t)*a.count) : a.n;
+}
 
 // Slot of entry e in this store, or -1 (counted) if it is outside.
 __device__ __forceinline__ int64_t slot_of(const UpdateArgs& a, int64_t e) {
@@ -70,12 +77,13 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
   const int64_t nth = (int64_t)gridDim.x * blockDim.x;
   uint32_t* tags = t.claims[0];
   float* leaves = t.levels[0];
+  const int64_t n = entries_of(a);
 
   // P0: new priorities, winner election (largest position wins), max priority
   uint32_t active = 0u, tmax = 0u, nbad = 0u, nforeign = 0u;
   for (int q = 0; q < kMaxPerThread; ++q) {
     const int64_t e = tid + (int64_t)q * nth;
-    if (e >= a.n) break;
+    if (e >= n) break;
     const int64_t i = slot_of(a, e);
     if (i < 0 || i >= t.capacity) {
       if (a.strict) ++nbad; else ++nforeign;
@@ -141,145 +149,7 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
   }
 }
 
-// ---------------------------------------------------------------- small update
-constexpr int kSmallMax = 1024;            // entries handled by the single CTA
-constexpr int kSmallPer = kSmallMax / kThreads;
-constexpr int kHashBits = 11;
-constexpr int kHash = 1 << kHashBits;      // >= 2 * kSmallMax: load factor <= 1/2
 constexpr uint32_t kEmpty = 0xffffffffu;
-constexpr size_t kSmallDynSmem = (size_t)(kThreads / 32) * PER_NODE_TILE;
-constexpr int kSlotsPerWarp = kHash / (kThreads / 32);
-
-__device__ __forceinline__ uint32_t hslot(uint32_t key) {
-  return (key * 2654435761u) >> (32 - kHashBits);
-}
-
-// Insert key (set semantics); returns its slot, or -1 if the table is full.
-__device__ __forceinline__ int hset_insert(uint32_t* keys, uint32_t key) {
-  uint32_t s = hslot(key);
-  for (int probe = 0; probe < kHash; ++probe) {
-    const uint32_t prev = atomicCAS(&keys[s], kEmpty, key);
-    if (prev == kEmpty || prev == key) return (int)s;
-    s = (s + 1) & (kHash - 1);
-  }
-  return -1;
-}
-
-__global__ void __launch_bounds__(kThreads) per_update_small_kernel(UpdateArgs a) {
-  per_wait_previous_grid();
-  const PerTree& t = a.t;
-  extern __shared__ __align__(16) unsigned char s_dyn[];  // per-warp node tiles
-  __shared__ uint32_t s_wkey[kHash];    // slot -> leaf index
-  __shared__ uint32_t s_wval[kHash];    // slot -> winning position + 1
-  __shared__ uint32_t s_set[2][kHash];  // touched nodes of the current / next level
-  __shared__ uint32_t s_list[kHash];  // the touched nodes of the current level
-  __shared__ int s_wcount[kThreads / 32];
-  __shared__ uint32_t s_max;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  unsigned char* tile = s_dyn + warp * PER_NODE_TILE;
-
-  // issue the input loads before clearing the tables
-  int64_t li[kSmallPer];
-  float tdv[kSmallPer];
-#pragma unroll
-  for (int q = 0; q < kSmallPer; ++q) {
-    const int64_t e = threadIdx.x + q * kThreads;
-    li[q] = e < a.n ? slot_of(a, e) : -1;
-    tdv[q] = e < a.n ? a.td[e] : 0.f;
-  }
-  for (int k = threadIdx.x; k < kHash; k += kThreads) {
-    s_wkey[k] = kEmpty;
-    s_wval[k] = 0u;
-    s_set[0][k] = kEmpty;
-    s_set[1][k] = kEmpty;
-  }
-  if (threadIdx.x == 0) s_max = 0u;
-  __syncthreads();
-
-  // P0: new priorities, winner election (largest position wins), max priority
-  int slot[kSmallPer];
-  float np[kSmallPer];
-  uint32_t tmax = 0u, nbad = 0u, nforeign = 0u;
-#pragma unroll
-  for (int q = 0; q < kSmallPer; ++q) {
-    const int64_t e = threadIdx.x + q * kThreads;
-    slot[q] = -1;
-    np[q] = 0.f;
-    if (e < a.n) {
-      if (li[q] < 0 || li[q] >= t.capacity) {
-        if (a.strict) ++nbad; else ++nforeign;
-      } else {
-        np[q] = new_priority(t, tdv[q]);
-        tmax = max(tmax, __float_as_uint(np[q]));
-        slot[q] = hset_insert(s_wkey, (uint32_t)li[q]);
-        if (slot[q] >= 0) atomicMax(&s_wval[slot[q]], (uint32_t)(e + 1));
-      }
-    }
-  }
-  if (nbad) {
-    per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
-    per_flag(t.status, PER_EVT_BAD_INDEX);
-  }
-  if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
-  if (lane == 0 && tmax) atomicMax(&s_max, tmax);
-  __syncthreads();
-  if (threadIdx.x == 0 && s_max) atomicMax(reinterpret_cast<unsigned int*>(t.max_priority), s_max);
-
-  // P1: winners write their leaf; collect touched chunks
-#pragma unroll
-  for (int q = 0; q < kSmallPer; ++q) {
-    const int64_t e = threadIdx.x + q * kThreads;
-    if (slot[q] >= 0 && s_wval[slot[q]] == (uint32_t)(e + 1)) {
-      t.levels[0][li[q]] = np[q];
-      hset_insert(s_set[0], (uint32_t)(li[q] >> PER_LOG_FANOUT));
-    }
-  }
-  __syncthreads();
-
-  // P2..: list the touched nodes of the level (each warp counts its share of
-  // the hash slots, then writes them at its offset: no shared counters),
-  // recompute them 32 per warp, and insert their parents into the next set
-  int cur = 0;
-  for (int L = 1; L < t.num_levels; ++L) {
-    uint32_t* set = s_set[cur];
-    uint32_t* nxt = s_set[cur ^ 1];
-    const bool more = L + 1 < t.num_levels;
-    int cnt = 0;
-#pragma unroll
-    for (int it = 0; it < kSlotsPerWarp / 32; ++it)
-      cnt += __popc(__ballot_sync(PER_FULL_MASK, set[warp * kSlotsPerWarp + it * 32 + lane] != kEmpty));
-    if (lane == 0) s_wcount[warp] = cnt;
-    __syncthreads();
-    int off = 0, total = 0;
-#pragma unroll
-    for (int w = 0; w < kThreads / 32; ++w) {
-      off += w < warp ? s_wcount[w] : 0;
-      total += s_wcount[w];
-    }
-#pragma unroll
-    for (int it = 0; it < kSlotsPerWarp / 32; ++it) {
-      const int k = warp * kSlotsPerWarp + it * 32 + lane;
-      const uint32_t node = set[k];
-      const uint32_t m = __ballot_sync(PER_FULL_MASK, node != kEmpty);
-      if (node != kEmpty) s_list[off + __popc(m & ((1u << lane) - 1u))] = node;
-      off += __popc(m);
-      set[k] = kEmpty;
-    }
-    __syncthreads();
-    for (int base = warp * 32; base < total; base += kThreads) {
-      const int k = base + lane;
-      const bool own = k < total;
-      const int64_t node = own ? (int64_t)s_list[k] : 0;
-      per_warp_recompute(t.levels[L - 1], t.levels[L], node, own, lane, tile);
-      if (own && more) hset_insert(nxt, (uint32_t)(node >> PER_LOG_FANOUT));
-    }
-    __syncthreads();
-    cur ^= 1;
-  }
-}
 
 // ---------------------------------------------------------------- prefetched update
 // Batches of up to kLMaxN indices whose lines fit in shared memory. The nodes
@@ -298,6 +168,7 @@ constexpr int kLHashBits = 10;
 constexpr int kLHash = 1 << kLHashBits;    // load factor <= 1/2
 constexpr int kLMaxT = 4;                  // tree levels above the leaves
 constexpr size_t kLinesSmemMax = 200 * 1024;  // shared memory the kernel may ask for
+constexpr int kLinesMaxPasses = 8;            // beyond this many passes: the grid path
 
 __device__ __forceinline__ uint32_t lslot(uint32_t key) {
   return (key * 2654435761u) >> (32 - kLHashBits);
@@ -339,7 +210,7 @@ __global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a
   const int warp = threadIdx.x >> 5;
   const uint32_t lbase = per_smem_addr_generic(lines);
 
-  // tables are cleared while the previous kernel may still run
+  // the first pass's tables are cleared while the previous kernel may still run
   for (int k = threadIdx.x; k < kLHash; k += kThreads) {
     wkey[k] = kEmpty;
     wval[k] = 0u;
@@ -348,146 +219,164 @@ __global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a
   if (threadIdx.x < kLMaxT) s_cnt[threadIdx.x] = 0;
   if (threadIdx.x == 0) s_max = 0u;
   per_wait_previous_grid();
-  int64_t li[kLPer];
-  float tdv[kLPer];
-#pragma unroll
-  for (int q = 0; q < kLPer; ++q) {
-    const int64_t e = threadIdx.x + q * kThreads;
-    li[q] = e < a.n ? slot_of(a, e) : -1;
-    tdv[q] = e < a.n ? a.td[e] : 0.f;
-  }
-  __syncthreads();
+  const int64_t n = entries_of(a);
 
-  // election (the last occurrence of a slot wins: largest position). Every
-  // valid entry also enters the node of each level above its leaf; the entry
-  // that adds a node first gives it a list position and fetches its line
-  // right away (the winner of a slot touches the same nodes)
-  int slot[kLPer], lslot0[kLPer];
-  float np[kLPer];
-  uint32_t tmax = 0u, nbad = 0u, nforeign = 0u;
-#pragma unroll
-  for (int q = 0; q < kLPer; ++q) {
-    const int64_t e = threadIdx.x + q * kThreads;
-    slot[q] = -1;
-    lslot0[q] = -1;
-    np[q] = 0.f;
-    bool valid = false;
-    if (e < a.n) {
-      if (li[q] < 0 || li[q] >= t.capacity) {
-        if (a.strict) ++nbad; else ++nforeign;
-      } else {
-        valid = true;
-        np[q] = new_priority(t, tdv[q]);
-        tmax = max(tmax, __float_as_uint(np[q]));
-        slot[q] = lset_insert(wkey, (uint32_t)li[q]);
-        if (slot[q] >= 0) atomicMax(&wval[slot[q]], (uint32_t)(e + 1));
+  // passes of `ncap` entries in order; a later pass overwrites an earlier
+  // one's leaves, so the last occurrence of a slot wins across passes too
+  for (int64_t c0 = 0; c0 < n; c0 += ncap) {
+    if (c0 > 0) {
+      __syncthreads();
+      for (int k = threadIdx.x; k < kLHash; k += kThreads) {
+        wkey[k] = kEmpty;
+        wval[k] = 0u;
+        for (int L = 0; L < T; ++L) skey[L * kLHash + k] = kEmpty;
       }
+      if (threadIdx.x < kLMaxT) s_cnt[threadIdx.x] = 0;
+      if (threadIdx.x == 0) s_max = 0u;
     }
-    uint32_t nd = valid ? (uint32_t)li[q] >> PER_LOG_FANOUT : 0u;
-    int below_p = -1;  // list position of the node entered at the level below, if new
-    for (int L = 0; L < T; ++L) {
-      int sl = -1;
-      bool fresh = false;
-      if (valid) {
-        uint32_t h = lslot(nd);
-        uint32_t* keys = skey + L * kLHash;
-        for (int probe = 0; probe < kLHash; ++probe) {
-          const uint32_t prev = atomicCAS(&keys[h], kEmpty, nd);
-          if (prev == kEmpty || prev == nd) {
-            sl = (int)h;
-            fresh = prev == kEmpty;
-            break;
-          }
-          h = (h + 1) & (kLHash - 1);
+    const int64_t c1 = min(c0 + ncap, n);
+    int64_t li[kLPer];
+    float tdv[kLPer];
+#pragma unroll
+    for (int q = 0; q < kLPer; ++q) {
+      const int64_t e = c0 + threadIdx.x + q * kThreads;
+      li[q] = e < c1 ? slot_of(a, e) : -1;
+      tdv[q] = e < c1 ? a.td[e] : 0.f;
+    }
+    __syncthreads();
+
+    // election (the last occurrence of a slot wins: largest position). Every
+    // valid entry also enters the node of each level above its leaf; the
+    // entry that adds a node first gives it a list position, and the warp
+    // fetches its new nodes' lines right away (the winner of a slot touches
+    // the same nodes)
+    int slot[kLPer], lslot0[kLPer];
+    float np[kLPer];
+    uint32_t tmax = 0u, nbad = 0u, nforeign = 0u;
+#pragma unroll
+    for (int q = 0; q < kLPer; ++q) {
+      const int64_t e = c0 + threadIdx.x + q * kThreads;
+      slot[q] = -1;
+      lslot0[q] = -1;
+      np[q] = 0.f;
+      bool valid = false;
+      if (e < c1) {
+        if (li[q] < 0 || li[q] >= t.capacity) {
+          if (a.strict) ++nbad; else ++nforeign;
+        } else {
+          valid = true;
+          np[q] = new_priority(t, tdv[q]);
+          tmax = max(tmax, __float_as_uint(np[q]));
+          slot[q] = lset_insert(wkey, (uint32_t)li[q]);
+          if (slot[q] >= 0) atomicMax(&wval[slot[q]], (uint32_t)(e + 1));
         }
       }
-      // list positions for the warp's new nodes: one shared counter add
-      const uint32_t m = __ballot_sync(PER_FULL_MASK, fresh);
-      int pbase = 0;
-      if (lane == 0 && m) pbase = atomicAdd(&s_cnt[L], __popc(m));
-      pbase = __shfl_sync(PER_FULL_MASK, pbase, 0);
-      const int newp = fresh ? pbase + __popc(m & ((1u << lane) - 1u)) : -1;
-      if (L == 0) lslot0[q] = sl;
-      if (below_p >= 0) pslot[(L - 1) * ncap + below_p] = (uint32_t)sl;  // parent of that node
-      const int nf = __popc(m);
-      if (fresh) {
-        list[L * ncap + newp] = nd;
-        spos[L * kLHash + sl] = (uint32_t)newp;
-        s_fresh[warp][newp - pbase] = (uint32_t)newp;
+      uint32_t nd = valid ? (uint32_t)li[q] >> PER_LOG_FANOUT : 0u;
+      int below_p = -1;  // list position of the node entered at the level below, if new
+      for (int L = 0; L < T; ++L) {
+        int sl = -1;
+        bool fresh = false;
+        if (valid) {
+          uint32_t h = lslot(nd);
+          uint32_t* keys = skey + L * kLHash;
+          for (int probe = 0; probe < kLHash; ++probe) {
+            const uint32_t prev = atomicCAS(&keys[h], kEmpty, nd);
+            if (prev == kEmpty || prev == nd) {
+              sl = (int)h;
+              fresh = prev == kEmpty;
+              break;
+            }
+            h = (h + 1) & (kLHash - 1);
+          }
+        }
+        // list positions for the warp's new nodes: one shared counter add
+        const uint32_t m = __ballot_sync(PER_FULL_MASK, fresh);
+        int pbase = 0;
+        if (lane == 0 && m) pbase = atomicAdd(&s_cnt[L], __popc(m));
+        pbase = __shfl_sync(PER_FULL_MASK, pbase, 0);
+        const int newp = fresh ? pbase + __popc(m & ((1u << lane) - 1u)) : -1;
+        if (L == 0) lslot0[q] = sl;
+        if (below_p >= 0) pslot[(L - 1) * ncap + below_p] = (uint32_t)sl;  // parent of that node
+        const int nf = __popc(m);
+        if (fresh) {
+          list[L * ncap + newp] = nd;
+          spos[L * kLHash + sl] = (uint32_t)newp;
+          s_fresh[warp][newp - pbase] = (uint32_t)newp;
+        }
+        __syncwarp();
+        // the warp fetches its new nodes' lines together, 4 lines (8 x 16 B
+        // each) per instruction
+        const float* clevel = t.levels[L];
+        for (int g = lane >> 3; g < nf; g += 4) {
+          const int p = (int)s_fresh[warp][g];
+          const int part = lane & 7;
+          per_cp_async16(lbase + (uint32_t)((L * ncap + p) * PER_LINE_STRIDE + part * 16),
+                         clevel + (int64_t)list[L * ncap + p] * PER_FANOUT + part * 4);
+        }
+        __syncwarp();
+        below_p = newp;
+        nd >>= PER_LOG_FANOUT;
       }
-      __syncwarp();
-      // the warp fetches its new nodes' lines together, 4 lines (8 x 16 B
-      // each) per instruction
-      const float* clevel = t.levels[L];
-      for (int g = lane >> 3; g < nf; g += 4) {
-        const int p = (int)s_fresh[warp][g];
-        const int part = lane & 7;
-        per_cp_async16(lbase + (uint32_t)((L * ncap + p) * PER_LINE_STRIDE + part * 16),
-                       clevel + (int64_t)list[L * ncap + p] * PER_FANOUT + part * 4);
-      }
-      __syncwarp();
-      below_p = newp;
-      nd >>= PER_LOG_FANOUT;
     }
-  }
-  if (nbad) {
-    per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
-    per_flag(t.status, PER_EVT_BAD_INDEX);
-  }
-  if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
-  if (lane == 0 && tmax) atomicMax(&s_max, tmax);
-  __syncthreads();
-  if (threadIdx.x == 0 && s_max) atomicMax(reinterpret_cast<unsigned int*>(t.max_priority), s_max);
-
-  // winners write their leaf; every thread waits for the lines it fetched
-  bool win[kLPer];
-#pragma unroll
-  for (int q = 0; q < kLPer; ++q) {
-    const int64_t e = threadIdx.x + q * kThreads;
-    win[q] = slot[q] >= 0 && wval[slot[q]] == (uint32_t)(e + 1);
-    if (win[q]) t.levels[0][li[q]] = np[q];
-  }
-  per_cp_async_wait_all();
-  __syncthreads();
-
-  // the winning leaves go into their chunk lines
-#pragma unroll
-  for (int q = 0; q < kLPer; ++q) {
-    if (win[q]) {
-      float* line = reinterpret_cast<float*>(lines + (size_t)spos[lslot0[q]] * PER_LINE_STRIDE);
-      line[li[q] & (PER_FANOUT - 1)] = np[q];
+    if (nbad) {
+      per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
+      per_flag(t.status, PER_EVT_BAD_INDEX);
     }
-  }
-  __syncthreads();
-
-  // level by level: sum each touched node's line, store it, patch it into
-  // its parent's line
-  for (int L = 0; L < T; ++L) {
-    for (int p = threadIdx.x; p < s_cnt[L]; p += kThreads) {
-      const uint32_t node = list[L * ncap + p];
-      const float4* row =
-          reinterpret_cast<const float4*>(lines + (size_t)(L * ncap + p) * PER_LINE_STRIDE);
-      float c[32];
+    if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 v = row[i];
-        c[4 * i] = v.x;
-        c[4 * i + 1] = v.y;
-        c[4 * i + 2] = v.z;
-        c[4 * i + 3] = v.w;
-      }
-      const float v = per_sum32_tree(c);
-      t.levels[L + 1][node] = v;
-      if (L + 1 < T) {
-        const uint32_t pp = spos[(L + 1) * kLHash + pslot[L * ncap + p]];
-        float* pline = reinterpret_cast<float*>(
-            lines + (size_t)((L + 1) * ncap + pp) * PER_LINE_STRIDE);
-        pline[node & (PER_FANOUT - 1)] = v;
+    for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
+    if (lane == 0 && tmax) atomicMax(&s_max, tmax);
+    __syncthreads();
+    if (threadIdx.x == 0 && s_max) atomicMax(reinterpret_cast<unsigned int*>(t.max_priority), s_max);
+
+    // winners write their leaf; every thread waits for the lines it fetched
+    bool win[kLPer];
+#pragma unroll
+    for (int q = 0; q < kLPer; ++q) {
+      const int64_t e = c0 + threadIdx.x + q * kThreads;
+      win[q] = slot[q] >= 0 && wval[slot[q]] == (uint32_t)(e + 1);
+      if (win[q]) t.levels[0][li[q]] = np[q];
+    }
+    per_cp_async_wait_all();
+    __syncthreads();
+
+    // the winning leaves go into their chunk lines
+#pragma unroll
+    for (int q = 0; q < kLPer; ++q) {
+      if (win[q]) {
+        float* line = reinterpret_cast<float*>(lines + (size_t)spos[lslot0[q]] * PER_LINE_STRIDE);
+        line[li[q] & (PER_FANOUT - 1)] = np[q];
       }
     }
     __syncthreads();
+
+    // level by level: sum each touched node's line, store it, patch it into
+    // its parent's line
+    for (int L = 0; L < T; ++L) {
+      for (int p = threadIdx.x; p < s_cnt[L]; p += kThreads) {
+        const uint32_t node = list[L * ncap + p];
+        const float4* row =
+            reinterpret_cast<const float4*>(lines + (size_t)(L * ncap + p) * PER_LINE_STRIDE);
+        float c[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 v = row[i];
+          c[4 * i] = v.x;
+          c[4 * i + 1] = v.y;
+          c[4 * i + 2] = v.z;
+          c[4 * i + 3] = v.w;
+        }
+        const float v = per_sum32_tree(c);
+        t.levels[L + 1][node] = v;
+        if (L + 1 < T) {
+          const uint32_t pp = spos[(L + 1) * kLHash + pslot[L * ncap + p]];
+          float* pline = reinterpret_cast<float*>(
+              lines + (size_t)((L + 1) * ncap + pp) * PER_LINE_STRIDE);
+          pline[node & (PER_FANOUT - 1)] = v;
+        }
+      }
+      __syncthreads();
+    }
   }
 }
 
@@ -596,11 +485,11 @@ int grid_for(const void* fn, int64_t work, int* grid) {
 
 int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int64_t n,
                       cudaStream_t stream) {
-  return per_launch_update_shard(t, 0, 1, idx, td, n, stream);
+  return per_launch_update_shard(t, 0, 1, idx, td, n, nullptr, stream);
 }
 
 int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, const int64_t* idx,
-                            const float* td, int64_t n, cudaStream_t stream) {
+                            const float* td, int64_t n, const int64_t* count, cudaStream_t stream) {
   UpdateArgs a;
   a.t = t;
   a.idx = idx;
@@ -608,25 +497,26 @@ int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, cons
   a.n = n;
   a.base = base;
   a.strict = strict;
+  a.count = reinterpret_cast<const unsigned long long*>(count);
+  // one CTA, passes of `ncap` entries with every line prefetched, while the
+  // passes stay few; larger batches take the grid path
   const int T = t.num_levels - 1;
-  const int ncap = (int)((n + 31) / 32 * 32);
-  if (n <= kLMaxN && T <= kLMaxT && lines_smem(T, ncap) <= kLinesSmemMax) {
+  int ncap = 0;
+  if (T <= kLMaxT) {
+    const int64_t want = n < kLMaxN ? n : kLMaxN;
+    for (int c = (int)((want + 31) / 32 * 32); c >= 32; c -= 32)
+      if (lines_smem(T, c) <= kLinesSmemMax) {
+        ncap = c;
+        break;
+      }
+  }
+  if (ncap > 0 && n <= (int64_t)kLinesMaxPasses * ncap) {
     const void* fl = (const void*)per_update_lines_kernel;
     const size_t smem = lines_smem(T, ncap);
-    int rc = per_set_smem(fl, lines_smem(kLMaxT, kLMaxN) < kLinesSmemMax ? lines_smem(kLMaxT, kLMaxN)
-                                                                         : kLinesSmemMax);
+    int rc = per_set_smem(fl, kLinesSmemMax);
     if (rc) return rc;
-    int nc = ncap;
-    void* args[] = {&a, &nc};
+    void* args[] = {&a, &ncap};
     cudaError_t e = per_launch(fl, 1, kThreads, smem, stream, args, false);
-    return e == cudaSuccess ? PER_OK : per_record_cuda(e);
-  }
-  if (n <= kSmallMax) {
-    const void* fs = (const void*)per_update_small_kernel;
-    int rc = per_set_smem(fs, kSmallDynSmem);
-    if (rc) return rc;
-    void* args[] = {&a};
-    cudaError_t e = per_launch(fs, 1, kThreads, kSmallDynSmem, stream, args, false);
     return e == cudaSuccess ? PER_OK : per_record_cuda(e);
   }
   const void* fn = (const void*)per_update_kernel;

@@ -112,6 +112,8 @@ SIGNATURES = {
     "per_sample_sharded_p2p": (ctypes.c_int, [ctypes.POINTER(Store), i32, i32, i64, vp, vp, i64,
                                               ctypes.c_float, vp, i64, vp, vp, vp, vp, vp]),
     "per_update_priorities_shard": (ctypes.c_int, [ctypes.POINTER(Store), i64, vp, vp, i64, vp]),
+    "per_update_priorities_shard_count": (ctypes.c_int, [ctypes.POINTER(Store), i64, vp, vp, i64, vp,
+                                                         vp]),
     "per_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "per_last_cuda_error": (ctypes.c_int, []),
     "per_abi_version": (ctypes.c_int, []),

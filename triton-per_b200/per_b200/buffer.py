@@ -174,12 +174,13 @@ class PERBuffer:
                    idx.data_ptr(), w.data_ptr())
         return dict(zip(self._names, out.split(self._dims, dim=1))), idx, w
 
-    def _outputs(self, b: int):
-        """Fresh [b, row_dim] rows and [b] weights (one float32 allocation), [b] indices."""
+    def _outputs(self, b: int, extra_idx: int = 0):
+        """Fresh [b, row_dim] rows and [b] weights (one float32 allocation) and
+        [b + extra_idx] int64 indices."""
         flat = torch.empty(b * (self.row_dim + 1), device=self.device)
         n = b * self.row_dim
-        return (flat[:n].view(b, self.row_dim), torch.empty(b, dtype=torch.int64, device=self.device),
-                flat[n:])
+        return (flat[:n].view(b, self.row_dim),
+                torch.empty(b + extra_idx, dtype=torch.int64, device=self.device), flat[n:])
 
     def _call(self, name, fn, *args) -> None:
         """fn(*args, stream) on this buffer's device and current stream; raises on error."""

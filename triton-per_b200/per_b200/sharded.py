@@ -101,24 +101,21 @@ class CudaShard:
 
     def sample_p2p(self, rank, world, base, mailboxes, rand, beta, rng=None, batch=None):
         b = rand.numel() if rng is None else batch
+        buf = self.buf
         dev = self.device
-        out = torch.empty(b, self.buf.row_dim, device=dev)
-        idx = torch.empty(b, dtype=torch.int64, device=dev)
-        w = torch.empty(b, device=dev)
+        out, idx_count, w = buf._outputs(b, extra_idx=1)
+        idx, count = idx_count[:b], idx_count[b:]
         pos = torch.empty(b, dtype=torch.int32, device=dev)
-        count = torch.empty(1, dtype=torch.int64, device=dev)
-        with torch.cuda.device(dev):
-            if rng is None:
-                _lib.check("per_sample_sharded_p2p", _lib.lib.per_sample_sharded_p2p(
-                    self.buf._store_ref, rank, world, base, mailboxes.data_ptr(), rand.data_ptr(),
-                    b, float(beta), out.data_ptr(), self.buf.row_dim, idx.data_ptr(),
-                    w.data_ptr(), pos.data_ptr(), count.data_ptr(), _stream_ptr(dev)))
-            else:
-                _lib.check("per_sample_sharded_p2p_rng", _lib.lib.per_sample_sharded_p2p_rng(
-                    self.buf._store_ref, rank, world, base, mailboxes.data_ptr(), rng[0],
-                    rng[1].data_ptr(), b, float(beta), out.data_ptr(), self.buf.row_dim,
-                    idx.data_ptr(), w.data_ptr(), pos.data_ptr(), count.data_ptr(),
-                    _stream_ptr(dev)))
+        if rng is None:
+            buf._call("per_sample_sharded_p2p", _lib.lib.per_sample_sharded_p2p, buf._store_ref,
+                      rank, world, base, mailboxes.data_ptr(), rand.data_ptr(), b, float(beta),
+                      out.data_ptr(), buf.row_dim, idx.data_ptr(), w.data_ptr(), pos.data_ptr(),
+                      count.data_ptr())
+        else:
+            buf._call("per_sample_sharded_p2p_rng", _lib.lib.per_sample_sharded_p2p_rng,
+                      buf._store_ref, rank, world, base, mailboxes.data_ptr(), rng[0],
+                      rng[1].data_ptr(), b, float(beta), out.data_ptr(), buf.row_dim,
+                      idx.data_ptr(), w.data_ptr(), pos.data_ptr(), count.data_ptr())
         return out, idx, w, pos, count
 
     def p2p_max_batch(self) -> int:
@@ -134,11 +131,14 @@ class CudaShard:
                 w.data_ptr(), count.data_ptr(), gmax.data_ptr(), w.numel(),
                 _stream_ptr(self.device)))
 
-    def update(self, base, idx, td):
-        with torch.cuda.device(self.device):
-            _lib.check("per_update_priorities_shard", _lib.lib.per_update_priorities_shard(
-                self.buf._store_ref, base, idx.data_ptr(), td.data_ptr(), idx.numel(),
-                _stream_ptr(self.device)))
+    def update(self, base, idx, td, count=None):
+        if count is None:
+            self.buf._call("per_update_priorities_shard", _lib.lib.per_update_priorities_shard,
+                           self.buf._store_ref, base, idx.data_ptr(), td.data_ptr(), idx.numel())
+        else:  # only the first *count entries (a sharded sample's owned draws)
+            self.buf._call("per_update_priorities_shard_count",
+                           _lib.lib.per_update_priorities_shard_count, self.buf._store_ref, base,
+                           idx.data_ptr(), td.data_ptr(), idx.numel(), count.data_ptr())
 
 
 class ShardedPERBuffer:
@@ -175,6 +175,8 @@ class ShardedPERBuffer:
         for name, d in fields.items():
             self._offsets[name] = (o, o + d)
             o += d
+        self._names = tuple(self._offsets)
+        self._dims = tuple(b - a for a, b in self._offsets.values())
         # identical uniform streams on every rank: the in-kernel Philox stream
         # (seed, device counter) of the CUDA shard; a torch generator for
         # other shard types
@@ -184,6 +186,7 @@ class ShardedPERBuffer:
         self._stats = torch.zeros(2, dtype=torch.float64, device=self.device)
         self._all_flat = torch.zeros(self.world * 2, dtype=torch.float64, device=self.device)
         self._all_stats = self._all_flat.view(self.world, 2)
+        self._last = None          # (idx, count) of the last sample on this rank
         self._mailbox = None       # own mailbox (device pointer)
         self._peer_boxes = []      # peers' mailboxes mapped into this process
         self._mailboxes = None     # int64[world] device array of mailbox pointers
@@ -297,6 +300,8 @@ class ShardedPERBuffer:
         if self.exchange == "p2p" and batch_size <= self.p2p_max_batch:
             out, idx, w, pos, count = self.shard.sample_p2p(
                 self.rank, self.world, self.base, self._mailboxes, None, beta, rng, batch_size)
+            self._last = (idx, count)
+            return ShardSample(self._views(out), idx, w, count, pos)
         else:
             self._exchange_stats()
             out, idx, w, pos, count, lmax = self.shard.sample(
@@ -304,8 +309,11 @@ class ShardedPERBuffer:
             if self.world > 1:
                 dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
             self.shard.normalize(w, count, lmax)
-        views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
-        return ShardSample(views, idx, w, count, pos)
+        self._last = (idx, count)
+        return ShardSample(self._views(out), idx, w, count, pos)
+
+    def _views(self, out):
+        return dict(zip(self._names, out.split(self._dims, dim=1)))
 
     def sample_from_uniforms(self, rand: torch.Tensor, beta: float = 0.4) -> ShardSample:
         """sample() with caller-provided global uniforms (identical on every rank)."""
@@ -330,7 +338,12 @@ class ShardedPERBuffer:
         """Apply the entries this rank owns (global indices; -1 = padding).
 
         route=True all-gathers every rank's entries first (same length on
-        every rank), so that TD errors computed on one rank reach the owner."""
+        every rank), so that TD errors computed on one rank reach the owner.
+        When `indices` is the idx tensor of this rank's last sample, only its
+        owned prefix (the sample's device count) is read."""
+        count = None
+        if not route and self._last is not None and indices is self._last[0]:
+            count = self._last[1]
         idx = indices.reshape(-1).to(device=self.device, dtype=torch.int64).contiguous()
         td = td_errors.detach().reshape(-1).to(device=self.device, dtype=torch.float32).contiguous()
         if idx.numel() != td.numel():
@@ -341,7 +354,10 @@ class ShardedPERBuffer:
             dist.all_gather_into_tensor(all_idx, idx, group=self.group)
             dist.all_gather_into_tensor(all_td, td, group=self.group)
             idx, td = all_idx, all_td
-        self.shard.update(self.base, idx, td)
+        if count is None:
+            self.shard.update(self.base, idx, td)
+        else:
+            self.shard.update(self.base, idx, td, count)
 
     def _exchange_stats(self) -> None:
         if self.world > 1:
