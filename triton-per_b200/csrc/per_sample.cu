@@ -37,6 +37,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "per_internal.h"
 
 namespace {
@@ -762,55 +764,110 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   }
 }
 
+// Launch shapes already chosen, per device, kernel, batch and store geometry
+// (small; a miss recomputes and overwrites round-robin).
+struct ShapeKey {
+  int dev;
+  const void* fn;
+  int64_t batch;
+  int32_t pre_bytes;
+  int32_t stage_bytes;
+  bool operator==(const ShapeKey& o) const {
+    return dev == o.dev && fn == o.fn && batch == o.batch && pre_bytes == o.pre_bytes &&
+           stage_bytes == o.stage_bytes;
+  }
+};
+struct Shape {
+  int nw;
+  int max_ctas;
+  int sms;
+};
+constexpr int kShapeSlots = 64;
+ShapeKey g_shape_key[kShapeSlots];
+Shape g_shape[kShapeSlots];
+int g_shape_used = 0, g_shape_next = 0;
+std::mutex g_shape_mu;
+
+bool shape_lookup(const ShapeKey& k, Shape* out) {
+  std::lock_guard<std::mutex> lk(g_shape_mu);
+  for (int i = 0; i < g_shape_used; ++i)
+    if (g_shape_key[i] == k) {
+      *out = g_shape[i];
+      return true;
+    }
+  return false;
+}
+
+void shape_store(const ShapeKey& k, const Shape& v) {
+  std::lock_guard<std::mutex> lk(g_shape_mu);
+  const int i = g_shape_next;
+  g_shape_next = (g_shape_next + 1) % kShapeSlots;
+  if (g_shape_used < kShapeSlots) ++g_shape_used;
+  g_shape_key[i] = k;
+  g_shape[i] = v;
+}
+
 template <int VEC, bool SHARDED>
 int launch_vec(SampleArgs a, cudaStream_t stream) {
   const void* fn = (const void*)per_sample_kernel<VEC, SHARDED>;
-  int sms = 148;
-  {
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  }
-  const int64_t warp_tiles = (a.batch + 31) / 32;
-  // a few rows per SM: cp.async has the lower latency; many: bulk copies
-  // keep more rows in flight
-  if (a.use_bulk && warp_tiles <= sms) a.use_bulk = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return per_record_cuda(e);
   const int n_top = (int)a.t.level_len[a.t.top_level];
   a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 15) & ~15;
-  int rc = per_set_smem(fn, (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes);
-  if (rc) return rc;
-  // compute warps per CTA: among the shapes that cover the batch in one wave
-  // of co-resident CTAs (one tile per warp), the one whose busiest SM holds
-  // the fewest warps (CTAs are spread round-robin over the SMs); ties go to
-  // fewer, larger CTAs (fewer prologues). Batches beyond one wave: 8 warps.
-  int64_t nw = kMaxWarps, best_cost = -1;
-  int max_ctas = 0;
-  for (int c = kMaxWarps; c >= 1; --c) {
-    int cap = 0;
-    rc = per_coresident_ctas(fn, (c + 1) * 32, (size_t)a.pre_bytes + (size_t)c * a.stage_bytes, &cap);
+  const int64_t warp_tiles = (a.batch + 31) / 32;
+  // the shape chosen for this kernel, batch and store geometry is cached
+  ShapeKey key{dev, fn, a.batch, a.pre_bytes, a.stage_bytes};
+  Shape sh;
+  if (!shape_lookup(key, &sh)) {
+    int sms = 148;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return per_record_cuda(e);
+    int rc = per_set_smem(fn, (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes);
     if (rc) return rc;
-    const int64_t tiles = (warp_tiles + c - 1) / c;
-    if (tiles > cap || tiles > kMaxGrid) continue;
-    const int64_t cost = (int64_t)c * ((tiles + sms - 1) / sms);
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      nw = c;
-      max_ctas = cap;
+    // compute warps per CTA: among the shapes that cover the batch in one
+    // wave of co-resident CTAs (one tile per warp), the one whose busiest SM
+    // holds the fewest warps (CTAs are spread round-robin over the SMs); ties
+    // go to fewer, larger CTAs (fewer prologues). Beyond one wave: 8 warps.
+    int64_t nw = kMaxWarps, best_cost = -1;
+    int max_ctas = 0;
+    for (int c = kMaxWarps; c >= 1; --c) {
+      int cap = 0;
+      rc = per_coresident_ctas(fn, (c + 1) * 32, (size_t)a.pre_bytes + (size_t)c * a.stage_bytes,
+                               &cap);
+      if (rc) return rc;
+      const int64_t tiles = (warp_tiles + c - 1) / c;
+      if (tiles > cap || tiles > kMaxGrid) continue;
+      const int64_t cost = (int64_t)c * ((tiles + sms - 1) / sms);
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        nw = c;
+        max_ctas = cap;
+      }
     }
+    if (best_cost < 0) {
+      rc = per_coresident_ctas(fn, (int)(nw + 1) * 32,
+                               (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes, &max_ctas);
+      if (rc) return rc;
+    }
+    sh.nw = (int)nw;
+    sh.max_ctas = max_ctas;
+    sh.sms = sms;
+    shape_store(key, sh);
   }
+  // a few rows per SM: cp.async has the lower latency; many: bulk copies
+  // keep more rows in flight
+  if (a.use_bulk && warp_tiles <= sh.sms) a.use_bulk = 0;
+  const int64_t nw = sh.nw;
   const int threads = (int)(nw + 1) * 32;
   const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
-  if (best_cost < 0) {
-    rc = per_coresident_ctas(fn, threads, smem, &max_ctas);
-    if (rc) return rc;
-  }
   a.num_tiles = (a.batch + nw * 32 - 1) / (nw * 32);
-  int64_t grid = a.num_tiles < max_ctas ? a.num_tiles : max_ctas;
+  int64_t grid = a.num_tiles < sh.max_ctas ? a.num_tiles : sh.max_ctas;
   if (grid > kMaxGrid) grid = kMaxGrid;
   if (grid < 1) grid = 1;
   if (a.p2p && a.num_tiles > grid) return PER_ERR_TOO_LARGE;  // one tile per warp
   void* args[] = {&a};
-  cudaError_t e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, grid > 1);
+  e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, grid > 1);
   return e == cudaSuccess ? PER_OK : per_record_cuda(e);
 }
 

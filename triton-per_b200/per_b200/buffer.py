@@ -36,6 +36,12 @@ def _stream_ptr(device: torch.device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def _current_stream(index: int) -> int:
+    """Handle of the current CUDA stream of device `index` (the cheap form of
+    torch.cuda.current_stream(index).cuda_stream)."""
+    return torch._C._cuda_getCurrentRawStream(index)
+
+
 class PERBuffer:
     def __init__(
         self,
@@ -175,21 +181,19 @@ class PERBuffer:
         return dict(zip(self._names, out.split(self._dims, dim=1))), idx, w
 
     def _outputs(self, b: int, extra_idx: int = 0):
-        """Fresh [b, row_dim] rows and [b] weights (one float32 allocation) and
-        [b + extra_idx] int64 indices."""
-        flat = torch.empty(b * (self.row_dim + 1), device=self.device)
-        n = b * self.row_dim
-        return (flat[:n].view(b, self.row_dim),
-                torch.empty(b + extra_idx, dtype=torch.int64, device=self.device), flat[n:])
+        """Fresh [b, row_dim] rows, [b] weights and [b + extra_idx] int64 indices."""
+        dev = self.device
+        return (torch.empty((b, self.row_dim), device=dev),
+                torch.empty(b + extra_idx, dtype=torch.int64, device=dev),
+                torch.empty(b, device=dev))
 
     def _call(self, name, fn, *args) -> None:
         """fn(*args, stream) on this buffer's device and current stream; raises on error."""
-        stream = torch.cuda.current_stream(self.device).cuda_stream
         if torch.cuda.current_device() != self._dev_index:
             with torch.cuda.device(self.device):
-                rc = fn(*args, stream)
+                rc = fn(*args, _current_stream(self._dev_index))
         else:
-            rc = fn(*args, stream)
+            rc = fn(*args, _current_stream(self._dev_index))
         if rc:
             _lib.check(name, rc)
 
@@ -226,6 +230,55 @@ class PERBuffer:
 
     def recover(self) -> None:
         """Reset the grid-barrier scratch and rebuild the sums after a reported timeout."""
+        self._scratch.zero_()
+        self.rebuild_sums()
+
+    # ------------------------------------------------------- checkpointing
+    STATE_VERSION = 1
+
+    def state_dict(self) -> dict:
+        """Everything needed to resume: configuration, rows, leaf priorities,
+        size and ring cursor, max priority and the position of the sample()
+        uniform stream. (The reference keeps none of this, buffer.py:52-63.)
+        The sum levels are not saved: they are exact functions of the leaves
+        and load_state_dict() rebuilds them bit for bit. Tensors stay on the
+        buffer's device; torch.save() them where they should go."""
+        sc = self._size_cursor.tolist()
+        return {
+            "version": self.STATE_VERSION,
+            "capacity": self.capacity,
+            "fields": dict(self.fields),
+            "alpha": self.alpha,
+            "eps": self.eps,
+            "size": int(sc[0]),
+            "cursor": int(sc[1]),
+            "storage": self.storage[: int(sc[0])].clone(),
+            "priorities": self.priorities[: self.capacity].clone(),
+            "max_priority": self._max_priority.clone(),
+            "rng_seed": self.rng_seed,
+            "rng_counter": int(self._rng_counter.item()),
+        }
+
+    def load_state_dict(self, state: dict) -> None:
+        """Restore a state_dict() into a buffer of the same capacity and fields."""
+        if state.get("version") != self.STATE_VERSION:
+            raise ValueError(f"unsupported buffer state version {state.get('version')!r}")
+        if state["capacity"] != self.capacity or dict(state["fields"]) != self.fields:
+            raise ValueError("buffer state has a different capacity or field layout")
+        if float(state["alpha"]) != float(self.alpha) or float(state["eps"]) != float(self.eps):
+            raise ValueError("buffer state has a different alpha or eps")
+        n = int(state["size"])
+        self._storage.zero_()
+        self.storage[:n].copy_(state["storage"].to(self.device))
+        self.priorities.zero_()
+        self.priorities[: self.capacity].copy_(state["priorities"].to(self.device))
+        self._max_priority.copy_(state["max_priority"].to(self.device))
+        self._size_cursor.copy_(torch.tensor([n, int(state["cursor"])], dtype=torch.int64))
+        self.size = n
+        self._cursor = int(state["cursor"])
+        self.rng_seed = int(state["rng_seed"])
+        self._rng_counter.fill_(int(state["rng_counter"]))
+        self._status.zero_()
         self._scratch.zero_()
         self.rebuild_sums()
 

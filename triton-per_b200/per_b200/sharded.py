@@ -359,6 +359,23 @@ class ShardedPERBuffer:
         else:
             self.shard.update(self.base, idx, td, count)
 
+    def state_dict(self) -> dict:
+        """This rank's shard (PERBuffer.state_dict) plus the sharding and the
+        shared uniform-stream position; each rank saves its own."""
+        if not isinstance(self.shard, CudaShard):
+            raise TypeError("state_dict needs the CUDA shard")
+        return {"rank": self.rank, "world": self.world, "capacity": self.capacity,
+                "seed": self.seed, "rng_counter": int(self._rng_counter.item()),
+                "shard": self.shard.buf.state_dict()}
+
+    def load_state_dict(self, state: dict) -> None:
+        if state["world"] != self.world or state["rank"] != self.rank or \
+                state["capacity"] != self.capacity:
+            raise ValueError("sharded state was saved by another rank or layout")
+        self.seed = int(state["seed"])
+        self._rng_counter.fill_(int(state["rng_counter"]))
+        self.shard.buf.load_state_dict(state["shard"])
+
     def _exchange_stats(self) -> None:
         if self.world > 1:
             self.shard.stats(self._stats)
