@@ -1,0 +1,100 @@
+// Python binding of the hot calls for torch tensors: one object per buffer
+// allocates the outputs with ATen, takes the current CUDA stream and calls
+// the C ABI (per_b200.h) directly. It replaces the ctypes round trip and the
+// Python-level allocation and view building of sample() / update_priorities()
+// (host cost per call, which bounds small-batch throughput outside CUDA
+// graphs). No kernels here: everything runs in libper_b200.so.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <string>
+#include <vector>
+
+#include "per_b200.h"
+
+namespace py = pybind11;
+
+namespace {
+
+class Engine {
+ public:
+  Engine(int64_t store, int64_t device, std::vector<std::string> names, std::vector<int64_t> dims,
+         int64_t rng_counter)
+      : store_(reinterpret_cast<const per_store_t*>(store)),
+        device_(static_cast<c10::DeviceIndex>(device)),
+        names_(std::move(names)),
+        dims_(std::move(dims)),
+        counter_(reinterpret_cast<uint64_t*>(rng_counter)) {
+    row_dim_ = 0;
+    for (int64_t d : dims_) row_dim_ += d;
+    py_names_ = py::list();
+    for (const auto& n : names_) py_names_.append(py::str(n));
+  }
+
+  // sample(batch, beta, seed) -> (rc, {name: view}, idx, w), uniforms drawn in the kernel
+  py::tuple sample(int64_t batch, double beta, uint64_t seed) {
+    c10::cuda::CUDAGuard guard(device_);
+    at::Tensor out, idx, w;
+    alloc(batch, &out, &idx, &w);
+    const int rc = per_sample_fused_rng(store_, seed, counter_, batch, static_cast<float>(beta),
+                                        out.data_ptr<float>(), row_dim_, idx.data_ptr<int64_t>(),
+                                        w.data_ptr<float>(), stream());
+    return py::make_tuple(rc, views(out), idx, w);
+  }
+
+  // sample_from(rand, beta) -> (rc, views, idx, w) with caller uniforms (float32, contiguous)
+  py::tuple sample_from(const at::Tensor& rand, double beta) {
+    c10::cuda::CUDAGuard guard(device_);
+    const int64_t batch = rand.numel();
+    at::Tensor out, idx, w;
+    alloc(batch, &out, &idx, &w);
+    const int rc = per_sample_fused(store_, rand.data_ptr<float>(), batch, static_cast<float>(beta),
+                                    out.data_ptr<float>(), row_dim_, idx.data_ptr<int64_t>(),
+                                    w.data_ptr<float>(), stream());
+    return py::make_tuple(rc, views(out), idx, w);
+  }
+
+  // update(idx int64, td float32), both contiguous on the device -> rc
+  int update(const at::Tensor& idx, const at::Tensor& td) {
+    c10::cuda::CUDAGuard guard(device_);
+    return per_update_priorities(store_, idx.data_ptr<int64_t>(), td.data_ptr<float>(),
+                                 idx.numel(), stream());
+  }
+
+ private:
+  void* stream() const { return c10::cuda::getCurrentCUDAStream(device_).stream(); }
+
+  void alloc(int64_t batch, at::Tensor* out, at::Tensor* idx, at::Tensor* w) const {
+    const auto f = at::TensorOptions().dtype(at::kFloat).device(at::kCUDA, device_);
+    *out = at::empty({batch, row_dim_}, f);
+    *idx = at::empty({batch}, f.dtype(at::kLong));
+    *w = at::empty({batch}, f);
+  }
+
+  py::dict views(const at::Tensor& out) const {
+    py::dict d;
+    const auto parts = out.split_with_sizes(dims_, 1);
+    for (size_t k = 0; k < parts.size(); ++k) d[py_names_[k]] = parts[k];
+    return d;
+  }
+
+  const per_store_t* store_;
+  c10::DeviceIndex device_;
+  std::vector<std::string> names_;
+  std::vector<int64_t> dims_;
+  py::list py_names_;
+  uint64_t* counter_;
+  int64_t row_dim_;
+};
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "torch-tensor binding of the per_b200 sample / update calls";
+  py::class_<Engine>(m, "Engine")
+      .def(py::init<int64_t, int64_t, std::vector<std::string>, std::vector<int64_t>, int64_t>())
+      .def("sample", &Engine::sample)
+      .def("sample_from", &Engine::sample_from)
+      .def("update", &Engine::update);
+}

@@ -27,6 +27,11 @@ import torch
 
 from . import _lib
 
+try:  # the torch-tensor binding of the hot calls (built beside libper_b200.so)
+    from . import _per_torch
+except ImportError:  # the ctypes calls below reach the same CUDA library
+    _per_torch = None
+
 BLOCK_P = 1024  # priorities per block (reference buffer.py:20)
 
 _BACKENDS = ("triton", "triton-unfused", "b200")
@@ -130,6 +135,9 @@ class PERBuffer:
         s.eps = float(eps)
         self._store = s
         self._store_ref = ctypes.byref(s)
+        self._engine = (_per_torch.Engine(ctypes.addressof(s), self._dev_index, list(self._names),
+                                          list(self._dims), self._rng_counter_ptr)
+                        if _per_torch is not None else None)
 
     # ------------------------------------------------------------------ add
     def add(self, batch: dict[str, torch.Tensor]) -> None:
@@ -161,6 +169,11 @@ class PERBuffer:
     def sample(self, batch_size: int, beta: float = 0.4):
         """Returns (fields: dict of views, indices, normalized IS weights)."""
         assert self.size > 0
+        if self._engine is not None:
+            rc, views, idx, w = self._engine.sample(int(batch_size), float(beta), self.rng_seed)
+            if rc:
+                _lib.check("per_sample_fused_rng", rc)
+            return views, idx, w
         b = int(batch_size)
         out, idx, w = self._outputs(b)
         self._call("per_sample_fused_rng", _lib.lib.per_sample_fused_rng, self._store_ref,
@@ -173,6 +186,11 @@ class PERBuffer:
         assert self.size > 0
         if rand.dtype != torch.float32 or rand.device != self.device or not rand.is_contiguous():
             rand = rand.to(device=self.device, dtype=torch.float32).contiguous()
+        if self._engine is not None:
+            rc, views, idx, w = self._engine.sample_from(rand, float(beta))
+            if rc:
+                _lib.check("per_sample_fused", rc)
+            return views, idx, w
         b = rand.numel()
         out, idx, w = self._outputs(b)
         self._call("per_sample_fused", _lib.lib.per_sample_fused, self._store_ref,
@@ -210,6 +228,11 @@ class PERBuffer:
         n = idx.numel()
         if n != td.numel():
             raise ValueError(f"{n} indices but {td.numel()} TD errors")
+        if self._engine is not None:
+            rc = self._engine.update(idx, td)
+            if rc:
+                _lib.check("per_update_priorities", rc)
+            return
         self._call("per_update_priorities", _lib.lib.per_update_priorities, self._store_ref,
                    idx.data_ptr(), td.data_ptr(), n)
 

@@ -55,15 +55,58 @@ def nvcc() -> str:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not needs_build():
-        return LIB
-    tmp = LIB + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-o", tmp, *sources()]
+    if force or needs_build():
+        tmp = LIB + ".tmp"
+        cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-o", tmp, *sources()]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+        os.replace(tmp, LIB)
+    build_binding(force=force, verbose=verbose)
+    return LIB
+
+
+# ---- the torch-tensor binding (csrc/per_torch.cpp -> per_b200/_per_torch*.so):
+# a C++ extension linked against libper_b200.so (found next to it at run time)
+BINDING_SRC = os.path.join(CSRC, "per_torch.cpp")
+
+
+def binding_path() -> str:
+    import sysconfig
+
+    return os.path.join(PKG, "_per_torch" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_binding(force: bool = False, verbose: bool = False) -> str:
+    import sysconfig
+
+    import torch
+    import torch.utils.cpp_extension as ext
+
+    out = binding_path()
+    deps = [BINDING_SRC, LIB, os.path.join(INCLUDE, "per_b200.h")]
+    if not force and os.path.exists(out) and all(os.path.getmtime(d) <= os.path.getmtime(out)
+                                                 for d in deps):
+        return out
+    cuda_home = ext.CUDA_HOME or "/usr/local/cuda"
+    incs = [os.path.join(os.path.dirname(torch.__file__), "include"),
+            os.path.join(os.path.dirname(torch.__file__), "include", "torch", "csrc", "api",
+                         "include"),
+            os.path.join(cuda_home, "include"), sysconfig.get_paths()["include"], INCLUDE]
+    libdir = os.path.join(os.path.dirname(torch.__file__), "lib")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-w",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_per_torch",
+           "-DTORCH_API_INCLUDE_EXTENSION_H",
+           *[f"-I{i}" for i in incs], BINDING_SRC, "-o", out + ".tmp",
+           f"-L{libdir}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+           "-ltorch_python", f"-Wl,-rpath,{libdir}",
+           f"-L{PKG}", "-lper_b200", "-Wl,-rpath,$ORIGIN"]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(out + ".tmp", out)
+    return out
 
 
 if __name__ == "__main__":
