@@ -58,6 +58,8 @@ BATCH = 256
 ROUNDS = 32
 BETA = 0.4
 SWEEP = [32, 128, 512, 2048, 8192, 32768, 65536]
+# beyond the configured sweep: several tiles per warp (more than one wave)
+SWEEP_LARGE = [131072, 262144]
 METRIC = "sampled transitions/s (sample+gather+IS)"
 UNIT = "transitions/s"
 
@@ -759,7 +761,7 @@ def main():
         graph = None
         heavy = make_store(dev, seed=5, priorities="heavy")
         sweep = []
-        for b in SWEEP:
+        for b in SWEEP + SWEEP_LARGE:
             us = kernel_time_us(heavy, b, reps=10, launches=8)
             gbs = algo_bytes(b, ROW_DIM) / (us * 1e-6) / 1e9
             sweep.append({"batch": b, "us": round(us, 3), "gbs": round(gbs, 1),

@@ -55,6 +55,34 @@ class Engine {
     return py::make_tuple(rc, views(out), idx, w);
   }
 
+  // sharded sample with the in-kernel exchange and uniforms:
+  // -> (rc, views, idx, w, pos, count) of this rank's owned draws
+  py::tuple sample_sharded_p2p(int32_t rank, int32_t world, int64_t shard_base, int64_t mailboxes,
+                               int64_t batch, double beta, uint64_t seed, int64_t counter) {
+    c10::cuda::CUDAGuard guard(device_);
+    const auto f = at::TensorOptions().dtype(at::kFloat).device(at::kCUDA, device_);
+    at::Tensor out = at::empty({batch, row_dim_}, f);
+    at::Tensor ic = at::empty({batch + 1}, f.dtype(at::kLong));  // idx, then the count
+    at::Tensor w = at::empty({batch}, f);
+    at::Tensor pos = at::empty({batch}, f.dtype(at::kInt));
+    at::Tensor idx = ic.narrow(0, 0, batch), count = ic.narrow(0, batch, 1);
+    const int rc = per_sample_sharded_p2p_rng(
+        store_, rank, world, shard_base, reinterpret_cast<void* const*>(mailboxes), seed,
+        reinterpret_cast<uint64_t*>(counter), batch, static_cast<float>(beta),
+        out.data_ptr<float>(), row_dim_, idx.data_ptr<int64_t>(), w.data_ptr<float>(),
+        pos.data_ptr<int32_t>(), count.data_ptr<int64_t>(), stream());
+    return py::make_tuple(rc, views(out), idx, w, pos, count);
+  }
+
+  // sharded update of the first *count entries (global indices) -> rc
+  int update_shard_count(int64_t base, const at::Tensor& idx, const at::Tensor& td,
+                         const at::Tensor& count) {
+    c10::cuda::CUDAGuard guard(device_);
+    return per_update_priorities_shard_count(store_, base, idx.data_ptr<int64_t>(),
+                                             td.data_ptr<float>(), idx.numel(),
+                                             count.data_ptr<int64_t>(), stream());
+  }
+
   // update(idx int64, td float32), both contiguous on the device -> rc
   int update(const at::Tensor& idx, const at::Tensor& td) {
     c10::cuda::CUDAGuard guard(device_);
@@ -96,5 +124,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def(py::init<int64_t, int64_t, std::vector<std::string>, std::vector<int64_t>, int64_t>())
       .def("sample", &Engine::sample)
       .def("sample_from", &Engine::sample_from)
-      .def("update", &Engine::update);
+      .def("update", &Engine::update)
+      .def("sample_sharded_p2p", &Engine::sample_sharded_p2p)
+      .def("update_shard_count", &Engine::update_shard_count);
 }

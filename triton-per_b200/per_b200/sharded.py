@@ -102,6 +102,13 @@ class CudaShard:
     def sample_p2p(self, rank, world, base, mailboxes, rand, beta, rng=None, batch=None):
         b = rand.numel() if rng is None else batch
         buf = self.buf
+        if rng is not None and buf._engine is not None:
+            rc, views, idx, w, pos, count = buf._engine.sample_sharded_p2p(
+                rank, world, base, mailboxes.data_ptr(), b, float(beta), rng[0],
+                rng[1].data_ptr())
+            if rc:
+                _lib.check("per_sample_sharded_p2p_rng", rc)
+            return views, idx, w, pos, count
         dev = self.device
         out, idx_count, w = buf._outputs(b, extra_idx=1)
         idx, count = idx_count[:b], idx_count[b:]
@@ -135,6 +142,10 @@ class CudaShard:
         if count is None:
             self.buf._call("per_update_priorities_shard", _lib.lib.per_update_priorities_shard,
                            self.buf._store_ref, base, idx.data_ptr(), td.data_ptr(), idx.numel())
+        elif self.buf._engine is not None:  # only the first *count entries
+            rc = self.buf._engine.update_shard_count(base, idx, td, count)
+            if rc:
+                _lib.check("per_update_priorities_shard_count", rc)
         else:  # only the first *count entries (a sharded sample's owned draws)
             self.buf._call("per_update_priorities_shard_count",
                            _lib.lib.per_update_priorities_shard_count, self.buf._store_ref, base,
@@ -301,7 +312,8 @@ class ShardedPERBuffer:
             out, idx, w, pos, count = self.shard.sample_p2p(
                 self.rank, self.world, self.base, self._mailboxes, None, beta, rng, batch_size)
             self._last = (idx, count)
-            return ShardSample(self._views(out), idx, w, count, pos)
+            views = out if isinstance(out, dict) else self._views(out)
+            return ShardSample(views, idx, w, count, pos)
         else:
             self._exchange_stats()
             out, idx, w, pos, count, lmax = self.shard.sample(
