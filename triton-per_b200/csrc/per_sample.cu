@@ -303,7 +303,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
 constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
 constexpr int kMaxGrid = PER_MAX_GRID;  // CTAs of one launch (scratch sized for it)
-constexpr int kAllToAllCtas = 32;  // max exchange: every CTA reads every slot up to this grid
+constexpr int kAllToAllCtas = 64;  // max exchange: every CTA reads every slot up to this grid
 
 template <int VEC, bool SHARDED>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(SampleArgs a) {
@@ -469,17 +469,17 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       const uint32_t tag = gen + 1u;
       if (lane == 0)
         per_st_release_u64(&sc->mx_slot[blockIdx.x], ((unsigned long long)tag << 32) | s_cta_max);
-      if (lane < (int)gridDim.x) {
-        unsigned long long v = per_ld_acquire_u64(&sc->mx_slot[lane]);
+      for (int c = lane; c < (int)gridDim.x; c += 32) {
+        unsigned long long v = per_ld_acquire_u64(&sc->mx_slot[c]);
         for (uint32_t it = 0; (uint32_t)(v >> 32) != tag; ++it) {
           if (it > PER_SPIN_LIMIT) {
             timed_out = true;
             break;
           }
           __nanosleep(PER_SPIN_SLEEP_NS);
-          v = per_ld_acquire_u64(&sc->mx_slot[lane]);
+          v = per_ld_acquire_u64(&sc->mx_slot[c]);
         }
-        mb = (uint32_t)v;
+        mb = max(mb, (uint32_t)v);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
