@@ -37,6 +37,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <math.h>
+
 #include <mutex>
 
 #include "per_internal.h"
@@ -74,6 +76,10 @@ struct SampleArgs {
   float* local_max;              // max unnormalised weight over this shard's draws
   PerMailbox* const* mailboxes;  // exchange over peer memory: every rank's mailbox
   int32_t p2p;                   // 1: exchange stats and max in-kernel through the mailboxes
+  // sharded, in-kernel exchange: each CTA routes its slice of `slice` global
+  // draws first and searches only the draws this shard owns
+  int32_t owned_only;
+  int32_t slice;
   // uniforms from the in-kernel Philox stream instead of `rand`
   int32_t use_rng;
   unsigned long long rng_seed;
@@ -303,6 +309,8 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
 constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
 constexpr int kMaxGrid = PER_MAX_GRID;  // CTAs of one launch (scratch sized for it)
+constexpr int kBarRouted = 3;  // compute warps: the CTA's owned draws are queued
+constexpr int kSliceMax = 1024;  // owned-only routing: global draws per CTA
 constexpr int kAllToAllCtas = 64;  // max exchange: every CTA reads every slot up to this grid
 
 template <int VEC, bool SHARDED>
@@ -316,6 +324,12 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   __shared__ double s_stats[SHARDED ? PER_MAX_SHARDS : 1][2];
   __shared__ unsigned long long s_seq;
   __shared__ unsigned long long s_owned;  // sharded: draws owned by this rank, all CTAs
+  // owned-only routing: this CTA's owned draws (offsets in its slice), and the
+  // output ranges its warps wrote (for the in-kernel normalisation)
+  __shared__ int32_t s_q[SHARDED ? kSliceMax : 1];
+  __shared__ int32_t s_qn;
+  __shared__ unsigned long long s_tbase[SHARDED ? kSliceMax / 32 : 1];
+  __shared__ int32_t s_tcnt[SHARDED ? kSliceMax / 32 : 1];
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -344,7 +358,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   const unsigned long long cbase = a.use_rng ? per_ld_relaxed_u64(a.rng_counter) : 0ull;
   int64_t tile = blockIdx.x;
   float rnd0 = 0.f;
-  if (!helper) {
+  if (!helper && !(SHARDED && a.owned_only)) {
     const int64_t j = tile * tile_draws + threadIdx.x;
     if (tile < a.num_tiles && j < a.batch) rnd0 = draw_uniform(a, cbase, j);
   }
@@ -380,7 +394,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     loc += head;
     const double incl = per_warp_scan_incl(loc, lane);
     if (lane == 31) s_wsum[warp] = incl;
-    if (threadIdx.x == 0) s_cta_max = 0u;
+    if (threadIdx.x == 0) {
+      s_cta_max = 0u;
+      if (SHARDED) s_qn = 0;
+    }
     __syncthreads();
     double run = incl - loc;
     for (int k = 0; k < warp; ++k) run += s_wsum[k];
@@ -584,19 +601,72 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   float w_last = 0.f;  // this lane's unnormalised weight in its last tile
   long long slot_last = -1;  // sharded: output slot of this lane's draw in its last tile
 
-  for (; tile < a.num_tiles; tile += gridDim.x) {
-    const bool last_tile = tile + gridDim.x >= a.num_tiles;
+  // owned-only routing (sharded, in-kernel exchange): the CTA routes its
+  // slice of the global batch, queues the draws this shard owns, and its
+  // warps then take the queue 32 draws at a time; tiles are local
+  const bool owned_mode = SHARDED && a.owned_only;
+  int64_t s0 = 0;
+  int64_t ntiles = a.num_tiles, tstep = gridDim.x;
+  if (owned_mode) {
+    s0 = (int64_t)blockIdx.x * a.slice;
+    const int64_t s1 = min(s0 + (int64_t)a.slice, a.batch);
+    const int tc = warp * 32 + lane;
+    for (int64_t j0 = s0; j0 < s1; j0 += (int64_t)nwarps * 32) {
+      const int64_t j = j0 + tc;
+      bool mine = false;
+      if (j < s1) {
+        const double r = (double)__fmul_rn(draw_uniform(a, cbase, j), total);
+        double S = 0.0;
+        int owner = -1, lastpos = 0;
+        for (int g = 0; g < a.world; ++g) {
+          const double tg = stats[2 * g];
+          if (tg > 0.0) lastpos = g;
+          S += tg;
+          if (owner < 0 && S > r) owner = g;
+        }
+        if (owner < 0) owner = lastpos;
+        mine = owner == a.rank && size > 0;
+      }
+      const uint32_t m = __ballot_sync(PER_FULL_MASK, mine);
+      int qb = 0;
+      if (lane == 0 && m) qb = atomicAdd(&s_qn, __popc(m));
+      qb = __shfl_sync(PER_FULL_MASK, qb, 0);
+      if (mine) s_q[qb + __popc(m & ((1u << lane) - 1u))] = (int32_t)(j - s0);
+    }
+    named_bar_sync(kBarRouted, nwarps * 32);
+    ntiles = (s_qn + 31) / 32;
+    tstep = nwarps;
+    tile = warp;
+    if (tile >= ntiles) {  // no draws for this warp: nothing to add to the CTA max
+      __syncwarp();
+      named_bar_arrive(kBarMaxReady, nthreads);
+    }
+  }
+
+  for (; tile < ntiles; tile += tstep) {
+    const bool last_tile = tile + tstep >= ntiles;
     const int64_t wj0 = tile * tile_draws + warp * 32;  // first draw of this warp
-    const int64_t j = wj0 + lane;
-    const bool ok = j < a.batch;
-    const float rnd = tile == blockIdx.x ? rnd0 : (ok ? draw_uniform(a, cbase, j) : 0.f);
+    int64_t j = wj0 + lane;
+    bool ok = j < a.batch;
+    if (owned_mode) {
+      const int64_t k = tile * 32 + lane;
+      ok = k < s_qn;
+      j = ok ? s0 + s_q[k] : 0;
+    }
+    const float rnd = owned_mode ? (ok ? draw_uniform(a, cbase, j) : 0.f)
+                      : tile == blockIdx.x ? rnd0
+                                           : (ok ? draw_uniform(a, cbase, j) : 0.f);
 
     const float u = __fmul_rn(rnd, total);
     double r = (double)u;
     bool own = ok;
     unsigned long long obase = 0ull;  // sharded: first output slot of this warp's draws
     uint32_t om = 0u;
-    if (SHARDED) {
+    if (owned_mode) {
+      r -= base64;
+      om = __ballot_sync(PER_FULL_MASK, own);
+      if (lane == 0 && om) obase = atomicAdd(&sc->draws[gen & 1u], (unsigned long long)__popc(om));
+    } else if (SHARDED) {
       // the shard whose range of the global prefix holds u (the last shard
       // with mass if u is at or past the total)
       double S = 0.0;
@@ -685,6 +755,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     int orank = 0;
     if (SHARDED) {  // compact the owned draws into [obase, obase + popc(om))
       obase = __shfl_sync(PER_FULL_MASK, obase, 0);
+      if (owned_mode && lane == 0) {
+        s_tbase[tile] = obase;
+        s_tcnt[tile] = __popc(om);
+      }
       orank = __popc(om & ((1u << lane) - 1u));
       if (own) s_rows[warp][orank] = (int32_t)i;
       row0 = (int64_t)obase;
@@ -748,8 +822,16 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   // (sharded: the caller normalises after reducing the max over the shards)
   named_bar_sync(kBarGmaxReady, nthreads);
   if (SHARDED) {
-    // in-kernel exchange (one tile per warp): normalise this lane's slot
-    if (a.p2p && slot_last >= 0) a.w[slot_last] = __fdiv_rn(w_last, s_gmax);
+    if (owned_mode) {  // normalise every weight this CTA wrote (its tiles' ranges)
+      const float gmax = s_gmax;
+      for (int64_t tl = warp; tl < ntiles; tl += nwarps) {
+        const int64_t o = (int64_t)s_tbase[tl];
+        if (lane < s_tcnt[tl]) a.w[o + lane] = __fdiv_rn(a.w[o + lane], gmax);
+      }
+    } else if (a.p2p && slot_last >= 0) {
+      // in-kernel exchange (one tile per warp): normalise this lane's slot
+      a.w[slot_last] = __fdiv_rn(w_last, s_gmax);
+    }
     // entries past the owned draws read as padding (-1) for a following update
     for (int64_t j = (int64_t)s_owned + (int64_t)blockIdx.x * tile_draws + warp * 32 + lane;
          j < a.batch; j += (int64_t)gridDim.x * tile_draws)
@@ -770,17 +852,19 @@ struct ShapeKey {
   int dev;
   const void* fn;
   int64_t batch;
+  int32_t world;  // owned-only routing: the number of shards; 0 otherwise
   int32_t pre_bytes;
   int32_t stage_bytes;
   bool operator==(const ShapeKey& o) const {
-    return dev == o.dev && fn == o.fn && batch == o.batch && pre_bytes == o.pre_bytes &&
-           stage_bytes == o.stage_bytes;
+    return dev == o.dev && fn == o.fn && batch == o.batch && world == o.world &&
+           pre_bytes == o.pre_bytes && stage_bytes == o.stage_bytes;
   }
 };
 struct Shape {
   int nw;
   int max_ctas;
   int sms;
+  int slice;  // owned-only routing: global draws per CTA
 };
 constexpr int kShapeSlots = 64;
 ShapeKey g_shape_key[kShapeSlots];
@@ -807,6 +891,23 @@ void shape_store(const ShapeKey& k, const Shape& v) {
   g_shape[i] = v;
 }
 
+// Owned-only routing: the largest slice (global draws per CTA, a multiple of
+// 32, at most kSliceMax) whose owned count stays within the CTA's c x 32
+// lanes with margin — mean + 4 standard deviations of a binomial with the
+// shard's expected share p (1.25 / world, for uneven masses) — so that every
+// warp has at most one tile (a warp with two would double the kernel's
+// latency chain).
+int owned_slice(int c, int world) {
+  const double p = world > 1 ? (1.25 / world < 1.0 ? 1.25 / world : 1.0) : 1.0;
+  int best = 32 * c;
+  for (int sl = 32 * c; sl <= kSliceMax; sl += 32) {
+    const double mean = sl * p, sd = sqrt(sl * p * (1.0 - p));
+    if (mean + 4.0 * sd > 32.0 * c) break;
+    best = sl;
+  }
+  return best;
+}
+
 template <int VEC, bool SHARDED>
 int launch_vec(SampleArgs a, cudaStream_t stream) {
   const void* fn = (const void*)per_sample_kernel<VEC, SHARDED>;
@@ -815,9 +916,10 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
   if (e != cudaSuccess) return per_record_cuda(e);
   const int n_top = (int)a.t.level_len[a.t.top_level];
   a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 15) & ~15;
+  if (a.world <= 1) a.owned_only = 0;  // one shard owns every draw: no routing pass
   const int64_t warp_tiles = (a.batch + 31) / 32;
-  // the shape chosen for this kernel, batch and store geometry is cached
-  ShapeKey key{dev, fn, a.batch, a.pre_bytes, a.stage_bytes};
+  // the shape chosen for this kernel, batch, world and store geometry is cached
+  ShapeKey key{dev, fn, a.batch, a.owned_only ? a.world : 0, a.pre_bytes, a.stage_bytes};
   Shape sh;
   if (!shape_lookup(key, &sh)) {
     int sms = 148;
@@ -825,17 +927,36 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     if (e != cudaSuccess) return per_record_cuda(e);
     int rc = per_set_smem(fn, (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes);
     if (rc) return rc;
-    // compute warps per CTA: among the shapes that cover the batch in one
-    // wave of co-resident CTAs (one tile per warp), the one whose busiest SM
-    // holds the fewest warps (CTAs are spread round-robin over the SMs); ties
-    // go to fewer, larger CTAs (fewer prologues). Beyond one wave: 8 warps.
-    int64_t nw = kMaxWarps, best_cost = -1;
-    int max_ctas = 0;
+    int64_t nw = kMaxWarps, best_cost = -1, best_grid = 0;
+    int max_ctas = 0, best_slice = 0;
     for (int c = kMaxWarps; c >= 1; --c) {
       int cap = 0;
       rc = per_coresident_ctas(fn, (c + 1) * 32, (size_t)a.pre_bytes + (size_t)c * a.stage_bytes,
                                &cap);
       if (rc) return rc;
+      if (a.owned_only) {
+        // owned-only: slices sized so that no warp gets two tiles; among the
+        // shapes that fit one wave, the fewest busy warps on the busiest SM,
+        // then the fewest CTAs
+        const int sl = owned_slice(c, a.world);
+        const int64_t grid = (a.batch + sl - 1) / sl;
+        if (grid > cap || grid > kMaxGrid) continue;
+        const double p = 1.25 / a.world < 1.0 ? 1.25 / a.world : 1.0;
+        const int64_t busy = (int64_t)((sl * p + 31.0) / 32.0) < c ? (int64_t)((sl * p + 31.0) / 32.0) : c;
+        const int64_t cost = busy * ((grid + sms - 1) / sms);
+        if (best_cost < 0 || cost < best_cost || (cost == best_cost && grid < best_grid)) {
+          best_cost = cost;
+          best_grid = grid;
+          nw = c;
+          max_ctas = cap;
+          best_slice = sl;
+        }
+        continue;
+      }
+      // compute warps per CTA: among the shapes that cover the batch in one
+      // wave of co-resident CTAs (one tile per warp), the one whose busiest
+      // SM holds the fewest warps (CTAs are spread round-robin over the SMs);
+      // ties go to fewer, larger CTAs (fewer prologues). Beyond one wave: 8.
       const int64_t tiles = (warp_tiles + c - 1) / c;
       if (tiles > cap || tiles > kMaxGrid) continue;
       const int64_t cost = (int64_t)c * ((tiles + sms - 1) / sms);
@@ -845,6 +966,7 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
         max_ctas = cap;
       }
     }
+    if (a.owned_only && best_cost < 0) return PER_ERR_TOO_LARGE;  // no one-wave shape
     if (best_cost < 0) {
       rc = per_coresident_ctas(fn, (int)(nw + 1) * 32,
                                (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes, &max_ctas);
@@ -853,19 +975,27 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     sh.nw = (int)nw;
     sh.max_ctas = max_ctas;
     sh.sms = sms;
+    sh.slice = best_slice;
     shape_store(key, sh);
   }
+  const int64_t nw = sh.nw;
   // a few rows per SM: cp.async has the lower latency; many: bulk copies
   // keep more rows in flight
-  if (a.use_bulk && warp_tiles <= sh.sms) a.use_bulk = 0;
-  const int64_t nw = sh.nw;
+  const int64_t busy_tiles = a.owned_only ? (warp_tiles + a.world - 1) / a.world : warp_tiles;
+  if (a.use_bulk && busy_tiles <= sh.sms) a.use_bulk = 0;
   const int threads = (int)(nw + 1) * 32;
   const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
   a.num_tiles = (a.batch + nw * 32 - 1) / (nw * 32);
-  int64_t grid = a.num_tiles < sh.max_ctas ? a.num_tiles : sh.max_ctas;
-  if (grid > kMaxGrid) grid = kMaxGrid;
-  if (grid < 1) grid = 1;
-  if (a.p2p && a.num_tiles > grid) return PER_ERR_TOO_LARGE;  // one tile per warp
+  int64_t grid;
+  if (a.owned_only) {
+    a.slice = sh.slice;
+    grid = (a.batch + a.slice - 1) / a.slice;
+  } else {
+    grid = a.num_tiles < sh.max_ctas ? a.num_tiles : sh.max_ctas;
+    if (grid > kMaxGrid) grid = kMaxGrid;
+    if (grid < 1) grid = 1;
+    if (a.p2p && a.num_tiles > grid) return PER_ERR_TOO_LARGE;  // one tile per warp
+  }
   void* args[] = {&a};
   e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, grid > 1);
   return e == cudaSuccess ? PER_OK : per_record_cuda(e);
@@ -914,6 +1044,8 @@ void fill_common(SampleArgs& a, const PerTree& t, const float* rand, int64_t bat
   a.local_max = nullptr;
   a.mailboxes = nullptr;
   a.p2p = 0;
+  a.owned_only = 0;
+  a.slice = 0;
   a.use_rng = 0;
   a.rng_seed = 0ull;
   a.rng_counter = nullptr;
@@ -1086,6 +1218,7 @@ int per_launch_sample_sharded_p2p(const PerTree& t, int32_t rank, int32_t world,
   a.count = reinterpret_cast<unsigned long long*>(count);
   a.mailboxes = mailboxes;
   a.p2p = 1;
+  a.owned_only = 1;
   set_rng(a, rng);
   return launch_any<true>(a, vec_width(t, out, out_stride), stream);
 }
