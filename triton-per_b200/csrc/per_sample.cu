@@ -265,14 +265,15 @@ __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stag
 __device__ __forceinline__ void gather_issue(const SampleArgs& a, unsigned char* stage,
                                              const int32_t* s_idx, int r0, int rn, int lane,
                                              uint64_t* mbar) {
-  const float* row = a.t.storage + (int64_t)s_idx[r0 + min(lane, rn - 1)] * a.t.row_stride;
   if (a.use_bulk) {
+    const float* row = a.t.storage + (int64_t)s_idx[r0 + min(lane, rn - 1)] * a.t.row_stride;
     per_fence_proxy_async_smem();  // earlier generic accesses of the tile before the bulk writes
     __syncwarp();
     if (lane == 0) per_mbar_arrive_expect_tx(mbar, (uint32_t)(rn * a.row_bytes));
     __syncwarp();
     if (lane < rn) per_bulk_load(stage + lane * a.row_bytes, row, (uint32_t)a.row_bytes, mbar);
   } else if (lane < rn) {
+    const float* row = a.t.storage + (int64_t)s_idx[r0 + lane] * a.t.row_stride;
     const uint32_t dst = per_smem_addr(stage + lane * a.row_bytes);
     const int cpb = a.cp_bytes;
     const int pieces = a.row_bytes / cpb;
@@ -358,10 +359,6 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   const unsigned long long cbase = a.use_rng ? per_ld_relaxed_u64(a.rng_counter) : 0ull;
   int64_t tile = blockIdx.x;
   float rnd0 = 0.f;
-  if (!helper && !(SHARDED && a.owned_only)) {
-    const int64_t j = tile * tile_draws + threadIdx.x;
-    if (tile < a.num_tiles && j < a.batch) rnd0 = draw_uniform(a, cbase, j);
-  }
 
   // ---- prologue (all warps): float64 exclusive prefix of the top level
   {
@@ -372,26 +369,35 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     const int end = min(beg + per, nv4);
     constexpr int kReg = 8;  // float4 per thread kept in registers
     float4 q[kReg];
-    double loc = 0.0;
 #pragma unroll
     for (int i = 0; i < kReg; ++i)
       q[i] = beg + i < end ? __ldg(topv4 + beg + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    // float64 sum of each float4 and their exclusive prefix within the thread,
+    // in short dependency chains (pairs, then a 3-step scan)
+    double f[kReg], pf[kReg];
+#pragma unroll
+    for (int i = 0; i < kReg; ++i)
+      f[i] = ((double)q[i].x + (double)q[i].y) + ((double)q[i].z + (double)q[i].w);
+#pragma unroll
+    for (int i = 0; i < kReg; ++i) pf[i] = i ? f[i - 1] : 0.0;
+#pragma unroll
+    for (int d = 1; d < kReg; d <<= 1) {
+      double nx[kReg];
+#pragma unroll
+      for (int i = 0; i < kReg; ++i) nx[i] = i >= d ? pf[i] + pf[i - d] : pf[i];
+#pragma unroll
+      for (int i = 0; i < kReg; ++i) pf[i] = nx[i];
+    }
+    double loc = pf[kReg - 1] + f[kReg - 1];
     for (int i0 = beg + kReg; i0 < end; ++i0) {  // long segments (few threads, big top level)
       const float4 v = __ldg(topv4 + i0);
-      loc += (double)v.x;
-      loc += (double)v.y;
-      loc += (double)v.z;
-      loc += (double)v.w;
+      loc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
     }
-    double head = 0.0;
-#pragma unroll
-    for (int i = 0; i < kReg; ++i) {
-      head += (double)q[i].x;
-      head += (double)q[i].y;
-      head += (double)q[i].z;
-      head += (double)q[i].w;
+    // this lane's first uniform, while the scan below waits on shuffles
+    if (!helper && !(SHARDED && a.owned_only)) {
+      const int64_t j = tile * tile_draws + threadIdx.x;
+      if (tile < a.num_tiles && j < a.batch) rnd0 = draw_uniform(a, cbase, j);
     }
-    loc += head;
     const double incl = per_warp_scan_incl(loc, lane);
     if (lane == 31) s_wsum[warp] = incl;
     if (threadIdx.x == 0) {
@@ -405,28 +411,29 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     for (int i = 0; i < kReg; ++i) {
       if (beg + i < end) {
         const int e = (beg + i) * 4;
-        s_pre[ppos(e)] = run;
-        run += (double)q[i].x;
-        s_pre[ppos(e + 1)] = run;
-        run += (double)q[i].y;
-        s_pre[ppos(e + 2)] = run;
-        run += (double)q[i].z;
-        s_pre[ppos(e + 3)] = run;
-        run += (double)q[i].w;
+        const double b = run + pf[i];
+        const double bx = b + (double)q[i].x;
+        const double bxy = bx + (double)q[i].y;
+        s_pre[ppos(e)] = b;
+        s_pre[ppos(e + 1)] = bx;
+        s_pre[ppos(e + 2)] = bxy;
+        s_pre[ppos(e + 3)] = bxy + (double)q[i].z;
       }
     }
+    double run2 = run + (pf[kReg - 1] + f[kReg - 1]);
     for (int i0 = beg + kReg; i0 < end; ++i0) {
       const float4 v = __ldg(topv4 + i0);
       const int e = i0 * 4;
-      s_pre[ppos(e)] = run;
-      run += (double)v.x;
-      s_pre[ppos(e + 1)] = run;
-      run += (double)v.y;
-      s_pre[ppos(e + 2)] = run;
-      run += (double)v.z;
-      s_pre[ppos(e + 3)] = run;
-      run += (double)v.w;
+      s_pre[ppos(e)] = run2;
+      run2 += (double)v.x;
+      s_pre[ppos(e + 1)] = run2;
+      run2 += (double)v.y;
+      s_pre[ppos(e + 2)] = run2;
+      run2 += (double)v.z;
+      s_pre[ppos(e + 3)] = run2;
+      run2 += (double)v.w;
     }
+    run = run + loc;
     if (end == nv4 && end > beg) s_pre[ppos(n_top)] = run;
     __syncthreads();
   }
