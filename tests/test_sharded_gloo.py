@@ -115,3 +115,65 @@ def test_sharded_union_equals_single_buffer():
     for rank, _, _, _, shard_leaves, *_ in results:
         np.testing.assert_allclose(shard_leaves, st.priorities[rank * shard_cap:(rank + 1) * shard_cap],
                                    rtol=1e-6)
+
+
+# ---------------------------------------------------------------- failures
+def _failure_worker(rank, world, port, mode, q):
+    for p in (os.path.dirname(HERE), os.path.join(os.path.dirname(HERE), "triton-per_b200"), HERE):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+
+    import torch.distributed as dist
+
+    from per_b200.sharded import ShardedPERBuffer
+    from shard_fake import CpuShard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    outcome = "ok"
+    try:
+        cap = 4000 if (mode == "mismatch" and rank == 1) else 6000
+        buf = ShardedPERBuffer(cap, {"x": 2}, device="cpu", seed=3,
+                               shard=CpuShard(-(-cap // world), {"x": 2}))
+        buf.add({"x": torch.zeros(100, 2)})
+        if mode == "dead" and rank == 1:
+            q.put((rank, "left"))  # this rank leaves between steps, before the collective
+            q.close()
+            q.join_thread()  # the message is out before the process ends
+            os._exit(0)
+        buf.sample(64)  # collective: exchanges the shard totals
+    except ValueError as e:
+        outcome = "ValueError: " + str(e)[:80]
+    except RuntimeError as e:  # the process group reports the missing peer
+        outcome = "RuntimeError: " + str(e)[:80]
+    q.put((rank, outcome))
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+@pytest.mark.parametrize("mode", ["mismatch", "dead"])
+def test_sharded_failures_surface_as_errors(mode):
+    """Host-side failure detection on gloo ranks: ranks that disagree on the
+    buffer layout all raise ValueError at construction; a rank that leaves
+    between steps makes the survivor's next collective raise (no hang)."""
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_failure_worker, args=(r, world, port, mode, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    if mode == "mismatch":
+        assert all(v.startswith("ValueError") for v in results.values()), results
+    else:
+        assert results[1] == "left"
+        assert results[0].startswith("RuntimeError"), results

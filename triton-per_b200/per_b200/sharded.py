@@ -175,6 +175,13 @@ class ShardedPERBuffer:
         self.fields = dict(fields)
         self.alpha = alpha
         self.eps = eps
+        if self.world > 1:  # every rank must build the same buffer (checked collectively)
+            mine = (int(capacity), tuple(self.fields.items()), float(alpha), float(eps), int(seed))
+            everyone = [None] * self.world
+            dist.all_gather_object(everyone, mine, group=group)
+            if any(o != everyone[0] for o in everyone):
+                raise ValueError("ShardedPERBuffer: ranks disagree on capacity, fields, alpha, eps "
+                                 f"or seed: {everyone}")
         self.shard_capacity = -(-capacity // self.world)
         self.base = self.rank * self.shard_capacity
         self.shard = shard if shard is not None else CudaShard(
