@@ -250,10 +250,10 @@ def sum_over_ranks(x: float, world: int) -> float:
 
 
 # ---------------------------------------------------------------- workload
-def make_store(device, seed, priorities="absnormal"):
+def make_store(device, seed, priorities="absnormal", storage_dtype=torch.float32):
     from per_b200 import PERBuffer
 
-    buf = PERBuffer(CAPACITY, FIELDS_74, device=device)
+    buf = PERBuffer(CAPACITY, FIELDS_74, device=device, storage_dtype=storage_dtype)
     g = torch.Generator(device=device).manual_seed(seed)
     chunk = 250_000
     for s in range(0, CAPACITY, chunk):
@@ -770,6 +770,16 @@ def main():
         storm = update_time_us(heavy, 65536, reps=5, launches=4)
         sweep.append({"update_storm_65536_us": round(storm, 2)})
         del heavy
+        torch.cuda.empty_cache()
+        # the same store with 16-bit (bfloat16) rows: half the gather bytes;
+        # GB/s counts the 16-bit row bytes (4 * row_dim + 16 per draw)
+        heavy16 = make_store(dev, seed=5, priorities="heavy", storage_dtype=torch.bfloat16)
+        for b in (8192, 65536, 262144):
+            us = kernel_time_us(heavy16, b, reps=10, launches=8)
+            gbs = b * (4 * ROW_DIM + 16) / (us * 1e-6) / 1e9
+            sweep.append({"batch_bf16_rows": b, "us": round(us, 3), "gbs": round(gbs, 1),
+                          "frac": round(gbs / peak, 4), "samples_per_s": round(b / (us * 1e-6))})
+        del heavy16
         torch.cuda.empty_cache()
         # wide rows: 2M x 4096 (32 GB), batch 1024, beta 0.6 (sample kernel +
         # whole-GPU row gather kernel per call)

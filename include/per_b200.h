@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define PER_ABI_VERSION 1
+#define PER_ABI_VERSION 2
 
 #define PER_BLOCK_P 1024   /* leaves per block: reference buffer.py:20 BLOCK_P */
 #define PER_FANOUT 32      /* children per tree node (= warp width) */
@@ -112,9 +112,17 @@ typedef struct per_store {
   int64_t scratch_bytes;
   float alpha;             /* buffer.py:29 */
   float eps;               /* buffer.py:30 */
+  /* bytes per row element: 4 (or 0) = float32 rows as in the reference;
+   * 2 = 16-bit rows (bfloat16 / float16, stored and gathered bit for bit,
+   * half the row bytes; not in the reference, whose rows are float32,
+   * buffer.py:52). With 2: row_dim, row_stride, every out_stride and every
+   * field's dim, stride and col_offset must be even (elements move in
+   * pairs), and `out` / field data point at 16-bit elements. */
+  int32_t elem_bytes;
 } per_store_t;
 
-/* One field of an add() batch: rows [n, dim] of float32 with a row stride. */
+/* One field of an add() batch: rows [n, dim] of the store's element type
+ * (float32, or 16-bit with elem_bytes 2) with a row stride. */
 typedef struct per_field {
   const float* data;
   int64_t dim;

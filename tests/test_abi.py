@@ -26,7 +26,7 @@ def test_library_exports_every_header_function():
 
 
 def test_abi_version():
-    assert _lib.lib.per_abi_version() == 1
+    assert _lib.lib.per_abi_version() == 2  # 2: per_store_t.elem_bytes (16-bit rows)
 
 
 C_PROBE = r"""

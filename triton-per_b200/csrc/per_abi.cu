@@ -9,7 +9,17 @@
 #include "per_b200.h"
 #include "per_internal.h"
 
+#include <nvtx3/nvToolsExt.h>
+
 namespace {
+
+// NVTX range around an entry point (profilers show each call; without a
+// profiler attached this is a few tens of nanoseconds)
+struct PerRange {
+  explicit PerRange(const char* name) { nvtxRangePushA(name); }
+  ~PerRange() { nvtxRangePop(); }
+};
+
 
 thread_local int g_last_cuda = 0;
 
@@ -56,9 +66,11 @@ PerTree tree_of(const per_store_t* s) {
   t.num_levels = s->num_levels;
   t.top_level = s->top_level;
   t.capacity = s->capacity;
+  // 16-bit rows travel as pairs of elements in 4-byte words: the kernels see
+  // float32-sized words (row sizes and strides in words)
   t.storage = s->storage;
-  t.row_dim = s->row_dim;
-  t.row_stride = s->row_stride;
+  t.row_dim = s->elem_bytes == 2 ? s->row_dim / 2 : s->row_dim;
+  t.row_stride = s->elem_bytes == 2 ? s->row_stride / 2 : s->row_stride;
   t.size_cursor = s->size_cursor;
   t.max_priority = s->max_priority;
   t.status = s->status;
@@ -86,7 +98,16 @@ int check_store(const per_store_t* s) {
   if (((uintptr_t)s->scratch) % 16 || ((uintptr_t)s->storage) % 4) return PER_ERR_MISALIGNED;
   if (s->row_dim < 1 || s->row_stride < s->row_dim) return PER_ERR_INVALID_ARGUMENT;
   if (!(s->eps >= 0.f) || !(s->alpha == s->alpha)) return PER_ERR_INVALID_ARGUMENT;
+  if (s->elem_bytes != 0 && s->elem_bytes != 4 && s->elem_bytes != 2) return PER_ERR_INVALID_ARGUMENT;
+  if (s->elem_bytes == 2 && (s->row_dim % 2 || s->row_stride % 2)) return PER_ERR_INVALID_ARGUMENT;
   return PER_OK;
+}
+
+// out_stride (elements of the store) in the kernels' 4-byte words; -1 if a
+// 16-bit store gets an odd stride
+int64_t out_words(const per_store_t* s, int64_t out_stride) {
+  if (s->elem_bytes != 2) return out_stride;
+  return out_stride % 2 ? -1 : out_stride / 2;
 }
 
 }  // namespace
@@ -249,10 +270,12 @@ int sample_fused(const per_store_t* store, const float* rand, const PerRng* rng,
   if (batch < 1) return PER_ERR_EMPTY;
   if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
   if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  const int64_t ow = out_words(store, out_stride);
+  if (ow < 0) return PER_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4 ||
       (rng && ((uintptr_t)rng->counter) % 8))
     return PER_ERR_MISALIGNED;
-  return per_launch_sample(tree_of(store), rand, rng, batch, beta, out, out_stride, idx, w,
+  return per_launch_sample(tree_of(store), rand, rng, batch, beta, out, ow, idx, w,
                            (cudaStream_t)stream);
 }
 
@@ -270,12 +293,14 @@ int sample_sharded(const per_store_t* store, int32_t rank, int32_t world, int64_
   if (batch < 1) return PER_ERR_EMPTY;
   if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
   if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  const int64_t ow = out_words(store, out_stride);
+  if (ow < 0) return PER_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4 ||
       ((uintptr_t)stats) % 8 || ((uintptr_t)pos) % 4 || ((uintptr_t)count) % 8 ||
       (rng && ((uintptr_t)rng->counter) % 8))
     return PER_ERR_MISALIGNED;
   return per_launch_sample_sharded(tree_of(store), rank, world, shard_base, stats, rand, rng,
-                                   batch, beta, out, out_stride, idx, w, pos, count, local_max,
+                                   batch, beta, out, ow, idx, w, pos, count, local_max,
                                    (cudaStream_t)stream);
 }
 
@@ -293,13 +318,15 @@ int sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world, in
   if (batch < 1) return PER_ERR_EMPTY;
   if (batch > ((int64_t)1 << 31)) return PER_ERR_TOO_LARGE;
   if (out_stride < store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  const int64_t ow = out_words(store, out_stride);
+  if (ow < 0) return PER_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)out) % 4 || ((uintptr_t)idx) % 8 || ((uintptr_t)w) % 4 || ((uintptr_t)rand) % 4 ||
       ((uintptr_t)pos) % 4 || ((uintptr_t)count) % 8 || ((uintptr_t)mailboxes) % 8 ||
       (rng && ((uintptr_t)rng->counter) % 8))
     return PER_ERR_MISALIGNED;
   return per_launch_sample_sharded_p2p(tree_of(store), rank, world, shard_base,
                                        reinterpret_cast<PerMailbox* const*>(mailboxes), rand, rng,
-                                       batch, beta, out, out_stride, idx, w, pos, count,
+                                       batch, beta, out, ow, idx, w, pos, count,
                                        (cudaStream_t)stream);
 }
 
@@ -307,6 +334,7 @@ int sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world, in
 
 int per_sample_fused(const per_store_t* store, const float* rand, int64_t batch, float beta,
                      float* out, int64_t out_stride, int64_t* idx, float* w, void* stream) {
+  PerRange range("per_sample_fused");
   if (!rand) return PER_ERR_NULL_POINTER;
   return sample_fused(store, rand, nullptr, batch, beta, out, out_stride, idx, w, stream);
 }
@@ -314,12 +342,14 @@ int per_sample_fused(const per_store_t* store, const float* rand, int64_t batch,
 int per_sample_fused_rng(const per_store_t* store, uint64_t seed, uint64_t* counter, int64_t batch,
                          float beta, float* out, int64_t out_stride, int64_t* idx, float* w,
                          void* stream) {
+  PerRange range("per_sample_fused_rng");
   const PerRng rng{(unsigned long long)seed, reinterpret_cast<unsigned long long*>(counter)};
   return sample_fused(store, nullptr, &rng, batch, beta, out, out_stride, idx, w, stream);
 }
 
 int per_update_priorities(const per_store_t* store, const int64_t* idx, const float* td, int64_t n,
                           void* stream) {
+  PerRange range("per_update_priorities");
   int rc = check_store(store);
   if (rc) return rc;
   if (!idx || !td) return PER_ERR_NULL_POINTER;
@@ -330,6 +360,7 @@ int per_update_priorities(const per_store_t* store, const int64_t* idx, const fl
 
 int per_add(const per_store_t* store, const per_field_t* fields, int32_t n_fields, int64_t n,
             void* stream) {
+  PerRange range("per_add");
   int rc = check_store(store);
   if (rc) return rc;
   if (n < 0) return PER_ERR_INVALID_ARGUMENT;
@@ -346,10 +377,21 @@ int per_add(const per_store_t* store, const per_field_t* fields, int32_t n_field
     covered += fd.dim;
   }
   if (covered != store->row_dim) return PER_ERR_INVALID_ARGUMENT;
+  if (store->elem_bytes == 2) {  // 16-bit rows: fields move as pairs of elements (words)
+    per_field_t words[PER_MAX_FIELDS];
+    for (int f = 0; f < n_fields; ++f) {
+      const per_field_t& fd = fields[f];
+      if (fd.dim % 2 || fd.stride % 2 || fd.col_offset % 2) return PER_ERR_INVALID_ARGUMENT;
+      if (((uintptr_t)fd.data) % 4) return PER_ERR_MISALIGNED;
+      words[f] = per_field_t{fd.data, fd.dim / 2, fd.stride / 2, fd.col_offset / 2};
+    }
+    return per_launch_add(tree_of(store), words, n_fields, n, (cudaStream_t)stream);
+  }
   return per_launch_add(tree_of(store), fields, n_fields, n, (cudaStream_t)stream);
 }
 
 int per_shard_stats(const per_store_t* store, double* out, void* stream) {
+  PerRange range("per_shard_stats");
   int rc = check_store(store);
   if (rc) return rc;
   if (!out) return PER_ERR_NULL_POINTER;
@@ -361,6 +403,7 @@ int per_sample_sharded(const per_store_t* store, int32_t rank, int32_t world, in
                        const double* stats, const float* rand, int64_t batch, float beta,
                        float* out, int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
                        int64_t* count, float* local_max, void* stream) {
+  PerRange range("per_sample_sharded");
   if (!rand) return PER_ERR_NULL_POINTER;
   return sample_sharded(store, rank, world, shard_base, stats, rand, nullptr, batch, beta, out,
                         out_stride, idx, w, pos, count, local_max, stream);
@@ -371,6 +414,7 @@ int per_sample_sharded_rng(const per_store_t* store, int32_t rank, int32_t world
                            uint64_t* counter, int64_t batch, float beta, float* out,
                            int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
                            int64_t* count, float* local_max, void* stream) {
+  PerRange range("per_sample_sharded_rng");
   const PerRng rng{(unsigned long long)seed, reinterpret_cast<unsigned long long*>(counter)};
   return sample_sharded(store, rank, world, shard_base, stats, nullptr, &rng, batch, beta, out,
                         out_stride, idx, w, pos, count, local_max, stream);
@@ -416,6 +460,7 @@ int per_sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world
                            int64_t shard_base, void* const* mailboxes, const float* rand,
                            int64_t batch, float beta, float* out, int64_t out_stride,
                            int64_t* idx, float* w, int32_t* pos, int64_t* count, void* stream) {
+  PerRange range("per_sample_sharded_p2p");
   if (!rand) return PER_ERR_NULL_POINTER;
   return sample_sharded_p2p(store, rank, world, shard_base, mailboxes, rand, nullptr, batch, beta,
                             out, out_stride, idx, w, pos, count, stream);
@@ -426,6 +471,7 @@ int per_sample_sharded_p2p_rng(const per_store_t* store, int32_t rank, int32_t w
                                uint64_t* counter, int64_t batch, float beta, float* out,
                                int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
                                int64_t* count, void* stream) {
+  PerRange range("per_sample_sharded_p2p_rng");
   const PerRng rng{(unsigned long long)seed, reinterpret_cast<unsigned long long*>(counter)};
   return sample_sharded_p2p(store, rank, world, shard_base, mailboxes, nullptr, &rng, batch, beta,
                             out, out_stride, idx, w, pos, count, stream);
@@ -439,6 +485,7 @@ int per_sample_sharded_p2p_max_batch(const per_store_t* store, int64_t* max_batc
 }
 
 int per_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap, void* stream) {
+  PerRange range("per_normalize");
   if (!w || !count || !gmax) return PER_ERR_NULL_POINTER;
   if (cap < 0) return PER_ERR_INVALID_ARGUMENT;
   if (cap == 0) return PER_OK;
@@ -447,6 +494,7 @@ int per_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap
 
 int per_update_priorities_shard(const per_store_t* store, int64_t base, const int64_t* idx,
                                 const float* td, int64_t n, void* stream) {
+  PerRange range("per_update_priorities_shard");
   int rc = check_store(store);
   if (rc) return rc;
   if (!idx || !td) return PER_ERR_NULL_POINTER;
@@ -459,6 +507,7 @@ int per_update_priorities_shard(const per_store_t* store, int64_t base, const in
 int per_update_priorities_shard_count(const per_store_t* store, int64_t base, const int64_t* idx,
                                       const float* td, int64_t n, const int64_t* count,
                                       void* stream) {
+  PerRange range("per_update_priorities_shard_count");
   int rc = check_store(store);
   if (rc) return rc;
   if (!idx || !td || !count) return PER_ERR_NULL_POINTER;
@@ -470,6 +519,7 @@ int per_update_priorities_shard_count(const per_store_t* store, int64_t base, co
 }
 
 int per_rebuild_sums(const per_store_t* store, void* stream) {
+  PerRange range("per_rebuild_sums");
   int rc = check_store(store);
   if (rc) return rc;
   return per_launch_rebuild(tree_of(store), (cudaStream_t)stream);

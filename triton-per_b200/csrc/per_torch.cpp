@@ -20,8 +20,9 @@ namespace {
 class Engine {
  public:
   Engine(int64_t store, int64_t device, std::vector<std::string> names, std::vector<int64_t> dims,
-         int64_t rng_counter)
+         int64_t rng_counter, int64_t row_dtype)
       : store_(reinterpret_cast<const per_store_t*>(store)),
+        row_dtype_(row_dtype == 1 ? at::kBFloat16 : row_dtype == 2 ? at::kHalf : at::kFloat),
         device_(static_cast<c10::DeviceIndex>(device)),
         names_(std::move(names)),
         dims_(std::move(dims)),
@@ -38,7 +39,7 @@ class Engine {
     at::Tensor out, idx, w;
     alloc(batch, &out, &idx, &w);
     const int rc = per_sample_fused_rng(store_, seed, counter_, batch, static_cast<float>(beta),
-                                        out.data_ptr<float>(), row_dim_, idx.data_ptr<int64_t>(),
+                                        rows(out), row_dim_, idx.data_ptr<int64_t>(),
                                         w.data_ptr<float>(), stream());
     return py::make_tuple(rc, views(out), idx, w);
   }
@@ -50,7 +51,7 @@ class Engine {
     at::Tensor out, idx, w;
     alloc(batch, &out, &idx, &w);
     const int rc = per_sample_fused(store_, rand.data_ptr<float>(), batch, static_cast<float>(beta),
-                                    out.data_ptr<float>(), row_dim_, idx.data_ptr<int64_t>(),
+                                    rows(out), row_dim_, idx.data_ptr<int64_t>(),
                                     w.data_ptr<float>(), stream());
     return py::make_tuple(rc, views(out), idx, w);
   }
@@ -61,7 +62,7 @@ class Engine {
                                int64_t batch, double beta, uint64_t seed, int64_t counter) {
     c10::cuda::CUDAGuard guard(device_);
     const auto f = at::TensorOptions().dtype(at::kFloat).device(at::kCUDA, device_);
-    at::Tensor out = at::empty({batch, row_dim_}, f);
+    at::Tensor out = at::empty({batch, row_dim_}, f.dtype(row_dtype_));
     at::Tensor ic = at::empty({batch + 1}, f.dtype(at::kLong));  // idx, then the count
     at::Tensor w = at::empty({batch}, f);
     at::Tensor pos = at::empty({batch}, f.dtype(at::kInt));
@@ -69,7 +70,7 @@ class Engine {
     const int rc = per_sample_sharded_p2p_rng(
         store_, rank, world, shard_base, reinterpret_cast<void* const*>(mailboxes), seed,
         reinterpret_cast<uint64_t*>(counter), batch, static_cast<float>(beta),
-        out.data_ptr<float>(), row_dim_, idx.data_ptr<int64_t>(), w.data_ptr<float>(),
+        rows(out), row_dim_, idx.data_ptr<int64_t>(), w.data_ptr<float>(),
         pos.data_ptr<int32_t>(), count.data_ptr<int64_t>(), stream());
     return py::make_tuple(rc, views(out), idx, w, pos, count);
   }
@@ -93,9 +94,12 @@ class Engine {
  private:
   void* stream() const { return c10::cuda::getCurrentCUDAStream(device_).stream(); }
 
+  // the output rows as the C ABI's pointer (float32 or 16-bit elements)
+  static float* rows(const at::Tensor& out) { return static_cast<float*>(out.data_ptr()); }
+
   void alloc(int64_t batch, at::Tensor* out, at::Tensor* idx, at::Tensor* w) const {
     const auto f = at::TensorOptions().dtype(at::kFloat).device(at::kCUDA, device_);
-    *out = at::empty({batch, row_dim_}, f);
+    *out = at::empty({batch, row_dim_}, f.dtype(row_dtype_));
     *idx = at::empty({batch}, f.dtype(at::kLong));
     *w = at::empty({batch}, f);
   }
@@ -108,6 +112,7 @@ class Engine {
   }
 
   const per_store_t* store_;
+  at::ScalarType row_dtype_;
   c10::DeviceIndex device_;
   std::vector<std::string> names_;
   std::vector<int64_t> dims_;
@@ -121,7 +126,8 @@ class Engine {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "torch-tensor binding of the per_b200 sample / update calls";
   py::class_<Engine>(m, "Engine")
-      .def(py::init<int64_t, int64_t, std::vector<std::string>, std::vector<int64_t>, int64_t>())
+      .def(py::init<int64_t, int64_t, std::vector<std::string>, std::vector<int64_t>, int64_t,
+                    int64_t>())
       .def("sample", &Engine::sample)
       .def("sample_from", &Engine::sample_from)
       .def("update", &Engine::update)

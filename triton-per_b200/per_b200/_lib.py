@@ -72,6 +72,7 @@ class Store(ctypes.Structure):
         ("scratch_bytes", i64),
         ("alpha", ctypes.c_float),
         ("eps", ctypes.c_float),
+        ("elem_bytes", i32),
     ]
 
 

@@ -35,6 +35,8 @@ except ImportError:  # the ctypes calls below reach the same CUDA library
 BLOCK_P = 1024  # priorities per block (reference buffer.py:20)
 
 _BACKENDS = ("triton", "triton-unfused", "b200")
+# row element types -> the binding's dtype code
+_ROW_DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 
 def _stream_ptr(device: torch.device):
@@ -56,7 +58,12 @@ class PERBuffer:
         alpha: float = 0.6,
         eps: float = 1e-6,
         backend: str = "triton",
+        storage_dtype: torch.dtype = torch.float32,
     ):
+        """`storage_dtype` torch.bfloat16 / torch.float16 keeps the rows in
+        16 bits (half the gather bytes; sampled rows come back in that dtype,
+        bit for bit; the row width must be even). Not in the reference, whose
+        rows are float32 (buffer.py:52)."""
         assert backend in _BACKENDS, (
             f"backend {backend!r}: this engine replaces the reference's triton backends; "
             f"use one of {_BACKENDS}")
@@ -72,6 +79,12 @@ class PERBuffer:
         self.backend = backend
 
         self.row_dim = sum(fields.values())
+        if storage_dtype not in _ROW_DTYPES:
+            raise ValueError(f"storage_dtype must be one of {list(_ROW_DTYPES)}, not {storage_dtype}")
+        self.storage_dtype = storage_dtype
+        self._elem_bytes = 2 if storage_dtype != torch.float32 else 4
+        if self._elem_bytes == 2 and self.row_dim % 2:
+            raise ValueError(f"16-bit rows need an even row width, not {self.row_dim}")
         self._offsets: dict[str, tuple[int, int]] = {}
         o = 0
         for name, d in fields.items():
@@ -87,8 +100,11 @@ class PERBuffer:
         self.top_level = int(lay.top_level)
 
         dev = self.device
-        self.row_stride = int(_lib.lib.per_row_stride(self.row_dim))
-        self._storage = torch.zeros(capacity, self.row_stride, device=dev)
+        if self._elem_bytes == 4:
+            self.row_stride = int(_lib.lib.per_row_stride(self.row_dim))
+        else:  # the recommended stride of the row's 4-byte words, in 16-bit elements
+            self.row_stride = 2 * int(_lib.lib.per_row_stride(self.row_dim // 2))
+        self._storage = torch.zeros(capacity, self.row_stride, device=dev, dtype=storage_dtype)
         self.storage = self._storage[:, : self.row_dim]
         self._levels = [torch.zeros(int(lay.level_len[k]), device=dev)
                         for k in range(self.num_levels)]
@@ -133,10 +149,12 @@ class PERBuffer:
         s.scratch_bytes = int(lay.scratch_bytes)
         s.alpha = float(alpha)
         s.eps = float(eps)
+        s.elem_bytes = self._elem_bytes
         self._store = s
         self._store_ref = ctypes.byref(s)
         self._engine = (_per_torch.Engine(ctypes.addressof(s), self._dev_index, list(self._names),
-                                          list(self._dims), self._rng_counter_ptr)
+                                          list(self._dims), self._rng_counter_ptr,
+                                          _ROW_DTYPES[storage_dtype])
                         if _per_torch is not None else None)
 
     # ------------------------------------------------------------------ add
@@ -146,12 +164,17 @@ class PERBuffer:
         if n == 0:
             return
         keep = []
-        fields = (_lib.Field * len(self._offsets))()
-        for f, (name, (a, b)) in enumerate(self._offsets.items()):
+        parts = []
+        for name, (a, b) in self._offsets.items():
             t = batch[name].reshape(n, -1)
             if t.shape[1] != b - a:
                 raise ValueError(f"field {name!r}: expected {b - a} values per row, got {t.shape[1]}")
-            t = t.to(device=self.device, dtype=torch.float32)
+            parts.append((t.to(device=self.device, dtype=self.storage_dtype), a, b))
+        if self._elem_bytes == 2:  # 16-bit rows move in pairs: one packed field per row
+            packed = torch.cat([t for t, _, _ in parts], dim=1).contiguous()
+            parts = [(packed, 0, self.row_dim)]
+        fields = (_lib.Field * len(parts))()
+        for f, (t, a, b) in enumerate(parts):
             if t.stride(1) != 1 or t.stride(0) < t.shape[1]:
                 t = t.contiguous()
             keep.append(t)
@@ -160,7 +183,7 @@ class PERBuffer:
             fields[f].stride = t.stride(0)
             fields[f].col_offset = a
         with torch.cuda.device(self.device):
-            _lib.check("per_add", _lib.lib.per_add(self._store_ref, fields, len(self._offsets), n,
+            _lib.check("per_add", _lib.lib.per_add(self._store_ref, fields, len(parts), n,
                                                    _stream_ptr(self.device)))
         self._cursor = int((self._cursor + n) % self.capacity)
         self.size = min(self.size + n, self.capacity)
@@ -201,7 +224,7 @@ class PERBuffer:
     def _outputs(self, b: int, extra_idx: int = 0):
         """Fresh [b, row_dim] rows, [b] weights and [b + extra_idx] int64 indices."""
         dev = self.device
-        return (torch.empty((b, self.row_dim), device=dev),
+        return (torch.empty((b, self.row_dim), device=dev, dtype=self.storage_dtype),
                 torch.empty(b + extra_idx, dtype=torch.int64, device=dev),
                 torch.empty(b, device=dev))
 
@@ -271,6 +294,7 @@ class PERBuffer:
             "version": self.STATE_VERSION,
             "capacity": self.capacity,
             "fields": dict(self.fields),
+            "storage_dtype": str(self.storage_dtype),
             "alpha": self.alpha,
             "eps": self.eps,
             "size": int(sc[0]),
@@ -288,6 +312,8 @@ class PERBuffer:
             raise ValueError(f"unsupported buffer state version {state.get('version')!r}")
         if state["capacity"] != self.capacity or dict(state["fields"]) != self.fields:
             raise ValueError("buffer state has a different capacity or field layout")
+        if state.get("storage_dtype", "torch.float32") != str(self.storage_dtype):
+            raise ValueError("buffer state has a different row dtype")
         if float(state["alpha"]) != float(self.alpha) or float(state["eps"]) != float(self.eps):
             raise ValueError("buffer state has a different alpha or eps")
         n = int(state["size"])
