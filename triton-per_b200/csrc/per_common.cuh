@@ -23,12 +23,13 @@
 struct PerScratch {
   uint32_t bar_count;    // arrivals at the current grid barrier
   uint32_t bar_gen;      // generation, bumped by the last arriver
-  uint32_t mx_count;     // sample, large grids: CTAs that published their max weight
+  uint32_t mx_count;     // unused (kept for the layout)
   uint32_t mx_gen;       // sample: launch generation, bumped once every CTA has published
-  uint32_t mx_bits[2];   // sample, large grids: running max weight bits, by generation parity
+  uint32_t mx_bits[2];   // unused (kept for the layout)
   unsigned long long draws[2];  // sharded sample: owned-draw counter, by generation parity
-  uint32_t pad[54];      // keep mx_slot[] 256-byte aligned
-  // sample, small grids: per CTA (generation + 1) << 32 | CTA max weight bits
+  unsigned long long mx_result;  // sample, large grids: (generation + 1) << 32 | max bits
+  uint32_t pad[52];      // keep mx_slot[] 256-byte aligned
+  // sample: per CTA (generation + 1) << 32 | CTA max weight bits
   unsigned long long mx_slot[PER_MAX_GRID / 2];
 };
 static_assert(sizeof(PerScratch) == PER_SCRATCH_BYTES, "scratch layout");

@@ -306,10 +306,27 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Max-exchange words: the sharded kernels also hand the owned-draw count
+// over through this exchange, so they publish with release / read with
+// acquire; the single-store kernels exchange only the max and use relaxed
+// accesses (a release store would first wait for the SM's outstanding row
+// traffic).
+template <bool ORDERED>
+__device__ __forceinline__ void mx_put(unsigned long long* p, unsigned long long v) {
+  if (ORDERED)
+    per_st_release_u64(p, v);
+  else
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+template <bool ORDERED>
+__device__ __forceinline__ unsigned long long mx_get(const unsigned long long* p) {
+  return ORDERED ? per_ld_acquire_u64(p) : per_ld_relaxed_u64(p);
+}
+
 // Named barriers between the compute warps and the CTA's helper warp.
 constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
 constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
-constexpr int kMaxGrid = PER_MAX_GRID;  // CTAs of one launch (scratch sized for it)
+constexpr int kMaxGrid = PER_MAX_GRID / 2;  // CTAs of one launch: one max slot each
 constexpr int kBarRouted = 3;  // compute warps: the CTA's owned draws are queued
 constexpr int kSliceMax = 1024;  // owned-only routing: global draws per CTA
 constexpr int kAllToAllCtas = 64;  // max exchange: every CTA reads every slot up to this grid
@@ -492,16 +509,16 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       // this launch's generation, and every helper reads all slots
       const uint32_t tag = gen + 1u;
       if (lane == 0)
-        per_st_release_u64(&sc->mx_slot[blockIdx.x], ((unsigned long long)tag << 32) | s_cta_max);
+        mx_put<SHARDED>(&sc->mx_slot[blockIdx.x], ((unsigned long long)tag << 32) | s_cta_max);
       for (int c = lane; c < (int)gridDim.x; c += 32) {
-        unsigned long long v = per_ld_acquire_u64(&sc->mx_slot[c]);
+        unsigned long long v = mx_get<SHARDED>(&sc->mx_slot[c]);
         for (uint32_t it = 0; (uint32_t)(v >> 32) != tag; ++it) {
           if (it > PER_SPIN_LIMIT) {
             timed_out = true;
             break;
           }
           __nanosleep(PER_SPIN_SLEEP_NS);
-          v = per_ld_acquire_u64(&sc->mx_slot[c]);
+          v = mx_get<SHARDED>(&sc->mx_slot[c]);
         }
         mb = max(mb, (uint32_t)v);
       }
@@ -512,26 +529,58 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
         if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
         sc->mx_gen = gen + 1u;
       }
-    } else if (lane == 0) {
-      // large grids: one running max and an arrival counter; the last CTA
-      // resets the other parity's words and releases the next generation
-      atomicMax(&sc->mx_bits[gen & 1u], s_cta_max);
-      const uint32_t old = per_atom_add_acq_rel(&sc->mx_count, 1u);
-      if (old == gridDim.x - 1) {
-        sc->mx_count = 0u;
-        sc->mx_bits[(gen + 1u) & 1u] = 0u;
-        if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
-        __threadfence();
-        per_st_release(&sc->mx_gen, gen + 1u);
-      }
-      for (uint32_t it = 0; per_ld_acquire(&sc->mx_gen) == gen; ++it) {
-        if (it > PER_SPIN_LIMIT) {
-          timed_out = true;
-          break;
+    } else {
+      // large grids: every CTA publishes its tagged slot (no read-modify-write
+      // chain on one word); CTA 0's helper reads them all and publishes the
+      // tagged max in one word, which the other helpers read
+      const uint32_t tag = gen + 1u;
+      if (lane == 0)
+        mx_put<SHARDED>(&sc->mx_slot[blockIdx.x], ((unsigned long long)tag << 32) | s_cta_max);
+      if (blockIdx.x == 0) {
+        // each lane polls its slots together (independent relaxed loads, one
+        // round trip per poll), then one acquire fence orders what follows
+        constexpr int kPer = kMaxGrid / 32;
+        static_assert(kPer <= 64, "one pending bit per slot of a lane");
+        unsigned long long pending = 0ull;  // bit i: slot lane + 32 i not seen yet
+        for (int i = 0; i < kPer && lane + 32 * i < (int)gridDim.x; ++i) pending |= 1ull << i;
+        for (uint32_t it = 0; __any_sync(PER_FULL_MASK, pending != 0ull); ++it) {
+          if (it > PER_SPIN_LIMIT) {
+            timed_out = true;
+            break;
+          }
+          unsigned long long left = pending;
+          while (left) {
+            const int i = __ffsll((long long)left) - 1;
+            left &= left - 1;
+            const unsigned long long v = per_ld_relaxed_u64(&sc->mx_slot[lane + 32 * i]);
+            if ((uint32_t)(v >> 32) == tag) {
+              mb = max(mb, (uint32_t)v);
+              pending &= ~(1ull << i);
+            }
+          }
+          if (pending) __nanosleep(PER_SPIN_SLEEP_NS);
         }
-        __nanosleep(PER_SPIN_SLEEP_NS);
+        if (SHARDED) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
+        if (lane == 0) {
+          sc->mx_bits[(gen + 1u) & 1u] = 0u;
+          if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
+          sc->mx_gen = gen + 1u;  // every CTA has read gen (all slots are in)
+          mx_put<SHARDED>(&sc->mx_result, ((unsigned long long)tag << 32) | mb);
+        }
+      } else if (lane == 0) {
+        unsigned long long v = mx_get<SHARDED>(&sc->mx_result);
+        for (uint32_t it = 0; (uint32_t)(v >> 32) != tag; ++it) {
+          if (it > PER_SPIN_LIMIT) {
+            timed_out = true;
+            break;
+          }
+          __nanosleep(PER_SPIN_SLEEP_NS);
+          v = mx_get<SHARDED>(&sc->mx_result);
+        }
+        mb = (uint32_t)v;
       }
-      mb = per_ld_relaxed_u32(&sc->mx_bits[gen & 1u]);
     }
     if (__any_sync(PER_FULL_MASK, timed_out) && lane == 0) {
       per_flag(t.status, PER_EVT_BARRIER_TIMEOUT);
