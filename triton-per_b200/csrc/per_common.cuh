@@ -27,9 +27,11 @@ struct PerScratch {
   uint32_t mx_gen;       // sample: launch generation, bumped once every CTA has published
   uint32_t mx_bits[2];   // unused (kept for the layout)
   unsigned long long draws[2];  // sharded sample: owned-draw counter, by generation parity
-  unsigned long long mx_result;  // sample, large grids: (generation + 1) << 32 | max bits
-  uint32_t pad[52];      // keep mx_slot[] 256-byte aligned
-  // sample: per CTA (generation + 1) << 32 | CTA max weight bits
+  unsigned long long mx_result;      // sample, large grids: (generation + 1) << 32 | max bits
+  unsigned long long mx_result_cnt;  // sample, large grids: (generation + 1) << 32 | owned draws
+  uint32_t pad[50];      // keep mx_slot[] 256-byte aligned
+  // sample: per CTA two words, (generation + 1) << 32 | CTA max weight bits
+  // and (generation + 1) << 32 | draws the CTA owns (sharded)
   unsigned long long mx_slot[PER_MAX_GRID / 2];
 };
 static_assert(sizeof(PerScratch) == PER_SCRATCH_BYTES, "scratch layout");
@@ -128,6 +130,10 @@ __device__ __forceinline__ unsigned long long per_globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+__device__ __forceinline__ void per_st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long per_ld_relaxed_u64(const unsigned long long* p) {

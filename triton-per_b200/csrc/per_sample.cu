@@ -306,27 +306,10 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// Max-exchange words: the sharded kernels also hand the owned-draw count
-// over through this exchange, so they publish with release / read with
-// acquire; the single-store kernels exchange only the max and use relaxed
-// accesses (a release store would first wait for the SM's outstanding row
-// traffic).
-template <bool ORDERED>
-__device__ __forceinline__ void mx_put(unsigned long long* p, unsigned long long v) {
-  if (ORDERED)
-    per_st_release_u64(p, v);
-  else
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-template <bool ORDERED>
-__device__ __forceinline__ unsigned long long mx_get(const unsigned long long* p) {
-  return ORDERED ? per_ld_acquire_u64(p) : per_ld_relaxed_u64(p);
-}
-
 // Named barriers between the compute warps and the CTA's helper warp.
 constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
 constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
-constexpr int kMaxGrid = PER_MAX_GRID / 2;  // CTAs of one launch: one max slot each
+constexpr int kMaxGrid = PER_MAX_GRID / 4;  // CTAs of one launch: one two-word slot each
 constexpr int kBarRouted = 3;  // compute warps: the CTA's owned draws are queued
 constexpr int kSliceMax = 1024;  // owned-only routing: global draws per CTA
 constexpr int kAllToAllCtas = 64;  // max exchange: every CTA reads every slot up to this grid
@@ -338,6 +321,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   __shared__ int32_t s_rows[kMaxWarps][32];
   __shared__ uint64_t s_mbar[kMaxWarps];
   __shared__ uint32_t s_cta_max;
+  __shared__ uint32_t s_cta_own;  // sharded: draws this CTA owns (compacted)
   __shared__ float s_gmax;
   __shared__ double s_stats[SHARDED ? PER_MAX_SHARDS : 1][2];
   __shared__ unsigned long long s_seq;
@@ -419,6 +403,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     if (lane == 31) s_wsum[warp] = incl;
     if (threadIdx.x == 0) {
       s_cta_max = 0u;
+      s_cta_own = 0u;
       if (SHARDED) s_qn = 0;
     }
     __syncthreads();
@@ -503,83 +488,76 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     // compute warps gather their rows
     named_bar_sync(kBarMaxReady, nthreads);
     uint32_t mb = 0u;
+    unsigned long long owned = 0ull;  // sharded: draws owned by this rank over all CTAs
     bool timed_out = false;
-    if (gridDim.x <= kAllToAllCtas) {
-      // small grids: every CTA publishes its max in its own slot, tagged with
-      // this launch's generation, and every helper reads all slots
-      const uint32_t tag = gen + 1u;
-      if (lane == 0)
-        mx_put<SHARDED>(&sc->mx_slot[blockIdx.x], ((unsigned long long)tag << 32) | s_cta_max);
-      for (int c = lane; c < (int)gridDim.x; c += 32) {
-        unsigned long long v = mx_get<SHARDED>(&sc->mx_slot[c]);
-        for (uint32_t it = 0; (uint32_t)(v >> 32) != tag; ++it) {
-          if (it > PER_SPIN_LIMIT) {
-            timed_out = true;
-            break;
-          }
-          __nanosleep(PER_SPIN_SLEEP_NS);
-          v = mx_get<SHARDED>(&sc->mx_slot[c]);
+    // every CTA publishes its max weight and (sharded) its owned-draw count in
+    // two words of its own slot, each tagged with this launch's generation;
+    // the data travel in the tagged words themselves, so the accesses are
+    // relaxed (no release store waiting on the SM's outstanding row traffic)
+    const uint32_t tag = gen + 1u;
+    unsigned long long* slots = sc->mx_slot;
+    if (lane == 0) {
+      per_st_relaxed_u64(&slots[2 * blockIdx.x], ((unsigned long long)tag << 32) | s_cta_max);
+      if (SHARDED) per_st_relaxed_u64(&slots[2 * blockIdx.x + 1], ((unsigned long long)tag << 32) | s_cta_own);
+    }
+    if (gridDim.x <= kAllToAllCtas || blockIdx.x == 0) {
+      // small grids: every helper reads all slots; large grids: CTA 0 does,
+      // each lane polling its slots together (one round trip per poll)
+      constexpr int kPer = kMaxGrid / 32;
+      static_assert(kPer <= 64, "one pending bit per slot of a lane");
+      unsigned long long pending = 0ull;  // bit i: slot lane + 32 i not seen yet
+      for (int i = 0; i < kPer && lane + 32 * i < (int)gridDim.x; ++i) pending |= 1ull << i;
+      for (uint32_t it = 0; __any_sync(PER_FULL_MASK, pending != 0ull); ++it) {
+        if (it > PER_SPIN_LIMIT) {
+          timed_out = true;
+          break;
         }
-        mb = max(mb, (uint32_t)v);
+        unsigned long long left = pending;
+        while (left) {
+          const int i = __ffsll((long long)left) - 1;
+          left &= left - 1;
+          const int c = lane + 32 * i;
+          const unsigned long long v = per_ld_relaxed_u64(&slots[2 * c]);
+          const unsigned long long n = SHARDED ? per_ld_relaxed_u64(&slots[2 * c + 1])
+                                               : ((unsigned long long)tag << 32);
+          if ((uint32_t)(v >> 32) == tag && (uint32_t)(n >> 32) == tag) {
+            mb = max(mb, (uint32_t)v);
+            owned += (uint32_t)n;
+            pending &= ~(1ull << i);
+          }
+        }
+        if (pending) __nanosleep(PER_SPIN_SLEEP_NS);
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
+      for (int o = 16; o > 0; o >>= 1) {
+        mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
+        owned += __shfl_xor_sync(PER_FULL_MASK, owned, o);
+      }
       if (lane == 0 && blockIdx.x == 0) {  // all CTAs have read gen: next generation
-        sc->mx_bits[(gen + 1u) & 1u] = 0u;
         if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
         sc->mx_gen = gen + 1u;
+        if (gridDim.x > kAllToAllCtas) {
+          if (SHARDED)
+            per_st_relaxed_u64(&sc->mx_result_cnt, ((unsigned long long)tag << 32) | (uint32_t)owned);
+          per_st_relaxed_u64(&sc->mx_result, ((unsigned long long)tag << 32) | mb);
+        }
       }
-    } else {
-      // large grids: every CTA publishes its tagged slot (no read-modify-write
-      // chain on one word); CTA 0's helper reads them all and publishes the
-      // tagged max in one word, which the other helpers read
-      const uint32_t tag = gen + 1u;
-      if (lane == 0)
-        mx_put<SHARDED>(&sc->mx_slot[blockIdx.x], ((unsigned long long)tag << 32) | s_cta_max);
-      if (blockIdx.x == 0) {
-        // each lane polls its slots together (independent relaxed loads, one
-        // round trip per poll), then one acquire fence orders what follows
-        constexpr int kPer = kMaxGrid / 32;
-        static_assert(kPer <= 64, "one pending bit per slot of a lane");
-        unsigned long long pending = 0ull;  // bit i: slot lane + 32 i not seen yet
-        for (int i = 0; i < kPer && lane + 32 * i < (int)gridDim.x; ++i) pending |= 1ull << i;
-        for (uint32_t it = 0; __any_sync(PER_FULL_MASK, pending != 0ull); ++it) {
-          if (it > PER_SPIN_LIMIT) {
-            timed_out = true;
-            break;
-          }
-          unsigned long long left = pending;
-          while (left) {
-            const int i = __ffsll((long long)left) - 1;
-            left &= left - 1;
-            const unsigned long long v = per_ld_relaxed_u64(&sc->mx_slot[lane + 32 * i]);
-            if ((uint32_t)(v >> 32) == tag) {
-              mb = max(mb, (uint32_t)v);
-              pending &= ~(1ull << i);
-            }
-          }
-          if (pending) __nanosleep(PER_SPIN_SLEEP_NS);
+    } else if (lane == 0) {
+      // large grids, CTAs other than 0: the totals CTA 0 published
+      for (uint32_t it = 0;; ++it) {
+        const unsigned long long v = per_ld_relaxed_u64(&sc->mx_result);
+        const unsigned long long n = SHARDED ? per_ld_relaxed_u64(&sc->mx_result_cnt)
+                                             : ((unsigned long long)tag << 32);
+        if ((uint32_t)(v >> 32) == tag && (uint32_t)(n >> 32) == tag) {
+          mb = (uint32_t)v;
+          owned = (uint32_t)n;
+          break;
         }
-        if (SHARDED) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
-        if (lane == 0) {
-          sc->mx_bits[(gen + 1u) & 1u] = 0u;
-          if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
-          sc->mx_gen = gen + 1u;  // every CTA has read gen (all slots are in)
-          mx_put<SHARDED>(&sc->mx_result, ((unsigned long long)tag << 32) | mb);
+        if (it > PER_SPIN_LIMIT) {
+          timed_out = true;
+          break;
         }
-      } else if (lane == 0) {
-        unsigned long long v = mx_get<SHARDED>(&sc->mx_result);
-        for (uint32_t it = 0; (uint32_t)(v >> 32) != tag; ++it) {
-          if (it > PER_SPIN_LIMIT) {
-            timed_out = true;
-            break;
-          }
-          __nanosleep(PER_SPIN_SLEEP_NS);
-          v = mx_get<SHARDED>(&sc->mx_result);
-        }
-        mb = (uint32_t)v;
+        __nanosleep(PER_SPIN_SLEEP_NS);
       }
     }
     if (__any_sync(PER_FULL_MASK, timed_out) && lane == 0) {
@@ -590,7 +568,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       s_gmax = __uint_as_float(mb);
       if (a.use_rng && blockIdx.x == 0) *a.rng_counter = cbase + (unsigned long long)a.batch;
       if (SHARDED) {  // every CTA has compacted its draws: the count is final
-        s_owned = per_ld_relaxed_u64(&sc->draws[gen & 1u]);
+        s_owned = owned;
         if (blockIdx.x == 0) {
           *a.count = s_owned;
           if (!a.p2p) *a.local_max = s_gmax;
@@ -721,7 +699,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     if (owned_mode) {
       r -= base64;
       om = __ballot_sync(PER_FULL_MASK, own);
-      if (lane == 0 && om) obase = atomicAdd(&sc->draws[gen & 1u], (unsigned long long)__popc(om));
+      if (lane == 0 && om) {
+        obase = atomicAdd(&sc->draws[gen & 1u], (unsigned long long)__popc(om));
+        atomicAdd(&s_cta_own, (uint32_t)__popc(om));
+      }
     } else if (SHARDED) {
       // the shard whose range of the global prefix holds u (the last shard
       // with mass if u is at or past the total)
@@ -739,7 +720,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       om = __ballot_sync(PER_FULL_MASK, own);
       // lane 0 reserves the warp's output slots; the result is broadcast only
       // after the search, so the atomic's round trip overlaps it
-      if (lane == 0 && om) obase = atomicAdd(&sc->draws[gen & 1u], (unsigned long long)__popc(om));
+      if (lane == 0 && om) {
+        obase = atomicAdd(&sc->draws[gen & 1u], (unsigned long long)__popc(om));
+        atomicAdd(&s_cta_own, (uint32_t)__popc(om));
+      }
     }
 
     // top level: binary search of the staged prefix
