@@ -10,7 +10,9 @@ Metric: sampled transitions per second (sample + gather + IS weights).
             around exactly K replays after W warm-up replays (max over ranks).
   e2e       the same loop through the public PERBuffer API, eager, with the
             step's inputs copied from pinned host memory and the sampled
-            batches (rows, idx, w) copied back to pinned host memory.
+            batches (rows, idx, w of every round, sampled into caller-owned
+            device slots with sample(..., out=)) copied back to pinned host
+            memory at the end of the step.
   roofline  the fused sample kernel alone on the same store: algorithmic
             bytes (8*row_dim + 16 per draw) over its CUDA-event launch time,
             against the measured HBM copy peak.
@@ -374,8 +376,11 @@ def update_time_us(buf, n, reps=20, launches=16, seed=8):
 
 
 def e2e_loop(buf, steps, warmup, world, seed=9):
-    """Public API, eager, host buffers: H2D of the step's inputs from pinned
-    memory, D2H of every sampled batch (rows, idx, w) into pinned memory."""
+    """Public API, eager, host buffers: H2D of the step's inputs (the added
+    transition, the TD errors of all rounds) from pinned memory; every round
+    samples into its slot of a device block through sample(..., out=) and
+    updates; the step ends with the D2H of every sampled batch (rows, idx, w
+    of all rounds: three copies) into pinned memory."""
     dev = buf.device
     g = np.random.default_rng(seed)
     h_row = {k: torch.from_numpy(g.standard_normal((1, d), dtype=np.float32)).pin_memory()
@@ -384,19 +389,23 @@ def e2e_loop(buf, steps, warmup, world, seed=9):
     h_rows = torch.empty(ROUNDS, BATCH, ROW_DIM).pin_memory()
     h_idx = torch.empty(ROUNDS, BATCH, dtype=torch.int64).pin_memory()
     h_w = torch.empty(ROUNDS, BATCH).pin_memory()
+    d_rows = torch.empty(ROUNDS, BATCH, ROW_DIM, device=dev)
+    d_idx = torch.empty(ROUNDS, BATCH, dtype=torch.int64, device=dev)
+    d_w = torch.empty(ROUNDS, BATCH, device=dev)
+    outs = [buf.sample_out(BATCH, rows=d_rows[r], idx=d_idx[r], w=d_w[r]) for r in range(ROUNDS)]
     h2d = sum(v.numel() * 4 for v in h_row.values()) + h_td.numel() * 4
     d2h = h_rows.numel() * 4 + h_idx.numel() * 8 + h_w.numel() * 4
 
     def step():
         row = {k: v.to(dev, non_blocking=True) for k, v in h_row.items()}
-        td = h_td.to(dev, non_blocking=True)
+        tds = h_td.to(dev, non_blocking=True).unbind(0)
         buf.add(row)
         for r in range(ROUNDS):
-            views, idx, w = buf.sample(BATCH, BETA)
-            buf.update_priorities(idx, td[r])
-            h_rows[r].copy_(packed_rows(views), non_blocking=True)
-            h_idx[r].copy_(idx, non_blocking=True)
-            h_w[r].copy_(w, non_blocking=True)
+            _, idx, _ = buf.sample(BATCH, BETA, out=outs[r])
+            buf.update_priorities(idx, tds[r])
+        h_rows.copy_(d_rows, non_blocking=True)
+        h_idx.copy_(d_idx, non_blocking=True)
+        h_w.copy_(d_w, non_blocking=True)
 
     for _ in range(warmup):
         step()

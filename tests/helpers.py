@@ -17,8 +17,10 @@ W_RTOL = 1e-6
 SUM_RTOL = 1e-5
 
 
-def make_buffer(capacity, fields, rows=None, leaves=None, alpha=0.6, eps=1e-6):
-    buf = PERBuffer(capacity, fields, device="cuda", alpha=alpha, eps=eps)
+def make_buffer(capacity, fields, rows=None, leaves=None, alpha=0.6, eps=1e-6,
+                storage_dtype=torch.float32):
+    buf = PERBuffer(capacity, fields, device="cuda", alpha=alpha, eps=eps,
+                    storage_dtype=storage_dtype)
     if rows is not None:
         buf.add({k: torch.as_tensor(v).cuda() for k, v in rows.items()})
     if leaves is not None:

@@ -306,6 +306,13 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Mailbox `g` of the in-kernel exchange (the pointer array is read-only
+// during the launch).
+__device__ __forceinline__ PerMailbox* mailbox_of(PerMailbox* const* mailboxes, int g) {
+  return reinterpret_cast<PerMailbox*>(
+      __ldg(reinterpret_cast<const unsigned long long*>(mailboxes) + g));
+}
+
 // Named barriers between the compute warps and the CTA's helper warp.
 constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
 constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
@@ -325,6 +332,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   __shared__ float s_gmax;
   __shared__ double s_stats[SHARDED ? PER_MAX_SHARDS : 1][2];
   __shared__ unsigned long long s_seq;
+  __shared__ PerMailbox* s_mine;
   __shared__ unsigned long long s_owned;  // sharded: draws owned by this rank, all CTAs
   // owned-only routing: this CTA's owned draws (offsets in its slice), and the
   // output ranges its warps wrote (for the in-kernel normalisation)
@@ -360,6 +368,13 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   const unsigned long long cbase = a.use_rng ? per_ld_relaxed_u64(a.rng_counter) : 0ull;
   int64_t tile = blockIdx.x;
   float rnd0 = 0.f;
+  // sharded, in-kernel exchange: this rank's mailbox and the sequence number
+  // of its last call (thread 0), and the peers' mailboxes (warp 0 of CTA 0,
+  // which publishes the statistics), loaded during the prologue
+  PerMailbox* mine = nullptr;
+  unsigned long long seq_prev = 0ull;
+  PerMailbox* peer_lo = nullptr;  // mailbox of rank `lane`
+  PerMailbox* peer_hi = nullptr;  // mailbox of rank `lane + 32`
 
   // ---- prologue (all warps): float64 exclusive prefix of the top level
   {
@@ -373,6 +388,18 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
 #pragma unroll
     for (int i = 0; i < kReg; ++i)
       q[i] = beg + i < end ? __ldg(topv4 + beg + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    // the mailbox loads go out behind the top level's (the sequence number
+    // depends on the mailbox pointer; it is needed only after the scan)
+    if (SHARDED && a.p2p) {
+      if (threadIdx.x == 0) {
+        mine = mailbox_of(a.mailboxes, a.rank);
+        seq_prev = *(volatile unsigned long long*)&mine->seq;
+      }
+      if (blockIdx.x == 0 && warp == 0) {
+        if (lane < a.world) peer_lo = mailbox_of(a.mailboxes, lane);
+        if (lane + 32 < a.world) peer_hi = mailbox_of(a.mailboxes, lane + 32);
+      }
+    }
     // float64 sum of each float4 and their exclusive prefix within the thread,
     // in short dependency chains (pairs, then a 3-step scan)
     double f[kReg], pf[kReg];
@@ -437,6 +464,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     }
     run = run + loc;
     if (end == nv4 && end > beg) s_pre[ppos(n_top)] = run;
+    if (SHARDED && a.p2p && threadIdx.x == 0) {
+      s_mine = mine;
+      s_seq = seq_prev + 1ull;
+    }
     __syncthreads();
   }
   const double* stats = a.stats;
@@ -444,9 +475,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     // ---- exchange the shard statistics over peer memory: CTA 0 publishes
     // this shard's (total, size) into slot `rank` of every rank's mailbox;
     // every CTA waits for all slots of its own mailbox to reach this call
-    PerMailbox* mine = a.mailboxes[a.rank];
-    if (threadIdx.x == 0) s_seq = *(volatile unsigned long long*)&mine->seq + 1ull;
-    __syncthreads();
+    mine = s_mine;
     const uint32_t tag = per_mail_tag(s_seq);
     if (warp == 0) {
       const double tot = s_pre[ppos(n_top)];
@@ -456,7 +485,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
         const unsigned long long sb = (unsigned long long)__double_as_longlong(szd);
         for (int g = lane; g < a.world; g += 32) {
           if (g == a.rank) continue;  // every CTA of this rank has its own values
-          unsigned long long* slot = a.mailboxes[g]->stats[a.rank];
+          unsigned long long* slot = (g < 32 ? peer_lo : peer_hi)->stats[a.rank];
           per_mail_put(slot + 0, (uint32_t)tb, tag);
           per_mail_put(slot + 1, (uint32_t)(tb >> 32), tag);
           per_mail_put(slot + 2, (uint32_t)sb, tag);
@@ -486,6 +515,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   if (helper) {
     // ---- helper warp: exchange the batch max with the other CTAs while the
     // compute warps gather their rows
+    if (SHARDED && a.p2p && blockIdx.x == 0) {  // peers' mailboxes, for the max put
+      if (lane < a.world) peer_lo = mailbox_of(a.mailboxes, lane);
+      if (lane + 32 < a.world) peer_hi = mailbox_of(a.mailboxes, lane + 32);
+    }
     named_bar_sync(kBarMaxReady, nthreads);
     uint32_t mb = 0u;
     unsigned long long owned = 0ull;  // sharded: draws owned by this rank over all CTAs
@@ -582,10 +615,11 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
       const float lmax = s_gmax;
       const unsigned long long seq = s_seq;
       const uint32_t mtag = per_mail_tag(seq);
-      PerMailbox* mine = a.mailboxes[a.rank];
+      mine = s_mine;
       if (blockIdx.x == 0) {
         for (int g = lane; g < a.world; g += 32)
-          if (g != a.rank) per_mail_put(&a.mailboxes[g]->max_w[a.rank], __float_as_uint(lmax), mtag);
+          if (g != a.rank)
+            per_mail_put(&(g < 32 ? peer_lo : peer_hi)->max_w[a.rank], __float_as_uint(lmax), mtag);
       }
       uint32_t gb = __float_as_uint(lmax);
       for (int g = lane; g < a.world; g += 32) {

@@ -44,6 +44,18 @@ class Engine {
     return py::make_tuple(rc, views(out), idx, w);
   }
 
+  // sample(batch, beta, seed) into caller-owned device buffers -> rc: rows
+  // (row_stride elements apart), idx (int64) and w (float32), checked by the
+  // caller once when the destination was made; nothing allocated, no views
+  int sample_into(int64_t batch, double beta, uint64_t seed, int64_t rows, int64_t row_stride,
+                  int64_t idx, int64_t w) {
+    c10::cuda::CUDAGuard guard(device_);
+    return per_sample_fused_rng(store_, seed, counter_, batch, static_cast<float>(beta),
+                                reinterpret_cast<float*>(rows), row_stride,
+                                reinterpret_cast<int64_t*>(idx), reinterpret_cast<float*>(w),
+                                stream());
+  }
+
   // sample_from(rand, beta) -> (rc, views, idx, w) with caller uniforms (float32, contiguous)
   py::tuple sample_from(const at::Tensor& rand, double beta) {
     c10::cuda::CUDAGuard guard(device_);
@@ -129,6 +141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def(py::init<int64_t, int64_t, std::vector<std::string>, std::vector<int64_t>, int64_t,
                     int64_t>())
       .def("sample", &Engine::sample)
+      .def("sample_into", &Engine::sample_into)
       .def("sample_from", &Engine::sample_from)
       .def("update", &Engine::update)
       .def("sample_sharded_p2p", &Engine::sample_sharded_p2p)

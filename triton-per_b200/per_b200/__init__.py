@@ -4,6 +4,6 @@ Drop-in for triton-per's `PERBuffer` (triton backend): PyTorch host code over
 hand-written sm_100a CUDA kernels behind a C ABI (include/per_b200.h).
 """
 
-from .buffer import BLOCK_P, PERBuffer
+from .buffer import BLOCK_P, PERBuffer, SampleOut
 
-__all__ = ["BLOCK_P", "PERBuffer"]
+__all__ = ["BLOCK_P", "PERBuffer", "SampleOut"]

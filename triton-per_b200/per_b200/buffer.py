@@ -189,9 +189,28 @@ class PERBuffer:
         self.size = min(self.size + n, self.capacity)
 
     # --------------------------------------------------------------- sample
-    def sample(self, batch_size: int, beta: float = 0.4):
-        """Returns (fields: dict of views, indices, normalized IS weights)."""
+    def sample(self, batch_size: int, beta: float = 0.4, out: "SampleOut | None" = None):
+        """Returns (fields: dict of views, indices, normalized IS weights).
+
+        With `out` (from sample_out()) the batch is written into that
+        caller-owned destination and its views are returned: no allocation
+        and no view building per call. The caller orders reuse of `out`
+        against readers of its previous contents (same stream, or events)."""
         assert self.size > 0
+        if out is not None:
+            if out.owner is not self or out.batch != int(batch_size):
+                raise ValueError("out was made by sample_out() of another buffer or batch size")
+            if self._engine is not None:
+                rc = self._engine.sample_into(out.batch, float(beta), self.rng_seed,
+                                              out._rows_ptr, out._row_stride, out._idx_ptr,
+                                              out._w_ptr)
+                if rc:
+                    _lib.check("per_sample_fused_rng", rc)
+            else:
+                self._call("per_sample_fused_rng", _lib.lib.per_sample_fused_rng, self._store_ref,
+                           self.rng_seed, self._rng_counter_ptr, out.batch, float(beta),
+                           out._rows_ptr, out._row_stride, out._idx_ptr, out._w_ptr)
+            return out.fields, out.idx, out.w
         if self._engine is not None:
             rc, views, idx, w = self._engine.sample(int(batch_size), float(beta), self.rng_seed)
             if rc:
@@ -203,6 +222,16 @@ class PERBuffer:
                    self.rng_seed, self._rng_counter_ptr, b, float(beta), out.data_ptr(),
                    self.row_dim, idx.data_ptr(), w.data_ptr())
         return dict(zip(self._names, out.split(self._dims, dim=1))), idx, w
+
+    def sample_out(self, batch_size: int, rows: torch.Tensor | None = None,
+                   idx: torch.Tensor | None = None, w: torch.Tensor | None = None) -> "SampleOut":
+        """A reusable destination for sample(batch_size, beta, out=...).
+
+        rows ([batch, row_dim], the storage dtype, unit column stride), idx
+        (int64 [batch]) and w (float32 [batch]) may be views into the caller's
+        own buffers, e.g. one slot of a [rounds, batch, ...] block that goes to
+        the host in one copy; missing ones are allocated here."""
+        return SampleOut(self, int(batch_size), rows, idx, w)
 
     def sample_from_uniforms(self, rand: torch.Tensor, beta: float = 0.4):
         """sample() with caller-provided uniforms in [0, 1) (float32, on the device)."""
@@ -334,3 +363,43 @@ class PERBuffer:
     def level(self, k: int) -> torch.Tensor:
         """Sums at tree level k (0 = leaves, 1 = 32-leaf chunks, 2 = block sums)."""
         return self._levels[k]
+
+
+class SampleOut:
+    """Caller-owned destination of one sampled batch (device tensors): the
+    rows with their per-field views, the indices and the weights. Made by
+    PERBuffer.sample_out(); checked once here so that sample(..., out=)
+    passes raw pointers only."""
+
+    def __init__(self, owner: PERBuffer, batch: int, rows=None, idx=None, w=None):
+        if batch < 1:
+            raise ValueError("batch must be positive")
+        dev = owner.device
+        if rows is None:
+            rows = torch.empty((batch, owner.row_dim), device=dev, dtype=owner.storage_dtype)
+        if idx is None:
+            idx = torch.empty(batch, dtype=torch.int64, device=dev)
+        if w is None:
+            w = torch.empty(batch, dtype=torch.float32, device=dev)
+        if rows.device != dev or idx.device != dev or w.device != dev:
+            raise ValueError(f"sample destinations must be on {dev}")
+        if rows.dtype != owner.storage_dtype or tuple(rows.shape) != (batch, owner.row_dim) \
+                or rows.stride(1) != 1 or rows.stride(0) < owner.row_dim:
+            raise ValueError(f"rows must be [{batch}, {owner.row_dim}] {owner.storage_dtype} "
+                             "with unit column stride")
+        if owner._elem_bytes == 2 and (rows.stride(0) % 2 or rows.data_ptr() % 4):
+            raise ValueError("16-bit rows: even row stride and 4-byte aligned start required")
+        if idx.dtype != torch.int64 or tuple(idx.shape) != (batch,) or not idx.is_contiguous():
+            raise ValueError(f"idx must be a contiguous int64 [{batch}] tensor")
+        if w.dtype != torch.float32 or tuple(w.shape) != (batch,) or not w.is_contiguous():
+            raise ValueError(f"w must be a contiguous float32 [{batch}] tensor")
+        self.owner = owner
+        self.batch = batch
+        self.rows = rows
+        self.idx = idx
+        self.w = w
+        self.fields = dict(zip(owner._names, rows.split(owner._dims, dim=1)))
+        self._rows_ptr = rows.data_ptr()
+        self._row_stride = rows.stride(0)
+        self._idx_ptr = idx.data_ptr()
+        self._w_ptr = w.data_ptr()
