@@ -12,7 +12,9 @@ Metric: sampled transitions per second (sample + gather + IS weights).
             step's inputs copied from pinned host memory and the sampled
             batches (rows, idx, w of every round, sampled into caller-owned
             device slots with sample(..., out=)) copied back to pinned host
-            memory at the end of the step.
+            memory at the end of the step, on a second stream that overlaps
+            the next step (double-buffered slots; the timed region ends
+            after the last read-back).
   roofline  the fused sample kernel alone on the same store: algorithmic
             bytes (8*row_dim + 16 per draw) over its CUDA-event launch time,
             against the measured HBM copy peak.
@@ -380,36 +382,55 @@ def e2e_loop(buf, steps, warmup, world, seed=9):
     transition, the TD errors of all rounds) from pinned memory; every round
     samples into its slot of a device block through sample(..., out=) and
     updates; the step ends with the D2H of every sampled batch (rows, idx, w
-    of all rounds: three copies) into pinned memory."""
+    of all rounds: three copies) into pinned memory, on a copy stream that
+    overlaps the next step's sampling (which uses the other block)."""
     dev = buf.device
     g = np.random.default_rng(seed)
     h_row = {k: torch.from_numpy(g.standard_normal((1, d), dtype=np.float32)).pin_memory()
              for k, d in FIELDS_74.items()}
     h_td = torch.from_numpy(np.abs(g.standard_normal((ROUNDS, BATCH))).astype(np.float32)).pin_memory()
-    h_rows = torch.empty(ROUNDS, BATCH, ROW_DIM).pin_memory()
-    h_idx = torch.empty(ROUNDS, BATCH, dtype=torch.int64).pin_memory()
-    h_w = torch.empty(ROUNDS, BATCH).pin_memory()
-    d_rows = torch.empty(ROUNDS, BATCH, ROW_DIM, device=dev)
-    d_idx = torch.empty(ROUNDS, BATCH, dtype=torch.int64, device=dev)
-    d_w = torch.empty(ROUNDS, BATCH, device=dev)
-    outs = [buf.sample_out(BATCH, rows=d_rows[r], idx=d_idx[r], w=d_w[r]) for r in range(ROUNDS)]
+    # two sets of device slots and host buffers: step k's read-back (on its
+    # own stream) overlaps step k+1's sampling, which uses the other set
+    sets = []
+    for _ in range(2):
+        d_rows = torch.empty(ROUNDS, BATCH, ROW_DIM, device=dev)
+        d_idx = torch.empty(ROUNDS, BATCH, dtype=torch.int64, device=dev)
+        d_w = torch.empty(ROUNDS, BATCH, device=dev)
+        sets.append({
+            "dev": (d_rows, d_idx, d_w),
+            "host": (torch.empty(ROUNDS, BATCH, ROW_DIM).pin_memory(),
+                     torch.empty(ROUNDS, BATCH, dtype=torch.int64).pin_memory(),
+                     torch.empty(ROUNDS, BATCH).pin_memory()),
+            "outs": [buf.sample_out(BATCH, rows=d_rows[r], idx=d_idx[r], w=d_w[r])
+                     for r in range(ROUNDS)],
+            "copied": None,
+        })
     h2d = sum(v.numel() * 4 for v in h_row.values()) + h_td.numel() * 4
-    d2h = h_rows.numel() * 4 + h_idx.numel() * 8 + h_w.numel() * 4
+    d2h = ROUNDS * BATCH * (ROW_DIM * 4 + 8 + 4)
+    st = torch.cuda.current_stream()
+    cs = torch.cuda.Stream(device=dev)
+    k = [0]
 
     def step():
-        row = {k: v.to(dev, non_blocking=True) for k, v in h_row.items()}
+        s = sets[k[0] % 2]
+        k[0] += 1
+        if s["copied"] is not None:  # its previous read-back has left the slots
+            st.wait_event(s["copied"])
+        row = {kk: v.to(dev, non_blocking=True) for kk, v in h_row.items()}
         tds = h_td.to(dev, non_blocking=True).unbind(0)
         buf.add(row)
         for r in range(ROUNDS):
-            _, idx, _ = buf.sample(BATCH, BETA, out=outs[r])
+            _, idx, _ = buf.sample(BATCH, BETA, out=s["outs"][r])
             buf.update_priorities(idx, tds[r])
-        h_rows.copy_(d_rows, non_blocking=True)
-        h_idx.copy_(d_idx, non_blocking=True)
-        h_w.copy_(d_w, non_blocking=True)
+        cs.wait_stream(st)
+        with torch.cuda.stream(cs):
+            for h, d in zip(s["host"], s["dev"]):
+                h.copy_(d, non_blocking=True)
+            s["copied"] = torch.cuda.Event()
+            s["copied"].record(cs)
 
     for _ in range(warmup):
         step()
-    st = torch.cuda.current_stream()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     barrier(world)
@@ -417,6 +438,7 @@ def e2e_loop(buf, steps, warmup, world, seed=9):
     a.record(st)
     for _ in range(steps):
         step()
+    st.wait_stream(cs)  # every read-back of the timed steps is inside the region
     b.record(st)
     torch.cuda.synchronize()
     barrier(world)
