@@ -408,6 +408,20 @@ __device__ __forceinline__ void per_fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Tensor Memory Accelerator gather of four rows (y0..y3, from column x) of
+// the 2-D tensor described by `tmap` (a tensor map in parameter or global
+// memory whose box is one row high) into four consecutive box rows of this
+// CTA's shared memory at `sdst` (128-byte aligned), completing on `bar`.
+// x times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void per_tma_gather4(void* sdst, const void* tmap, int x, int y0, int y1,
+                                                int y2, int y3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(per_smem_addr(sdst)),
+      "l"(tmap), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(per_smem_addr(bar))
+      : "memory");
+}
+
 // Bulk copy global -> this CTA's shared memory, completing on `bar`.
 // Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void per_bulk_load(void* sdst, const void* gsrc, uint32_t bytes,

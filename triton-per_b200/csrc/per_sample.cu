@@ -34,10 +34,14 @@
 // u = rand * total (fp32 product, as torch computes it), with prefixes in
 // float64 so the result equals a search over exact prefixes; rounding
 // fallbacks and empty-slot walk-backs are counted in the status words.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <mutex>
 
@@ -63,6 +67,8 @@ struct SampleArgs {
   int32_t stage_bytes;     // per-warp staging bytes
   int32_t row_bytes;       // staged bytes per row (bulk: row_dim*4 rounded up to 16)
   int32_t use_bulk;        // rows are 16-byte aligned: gather with bulk copies
+  int32_t gather4;         // bulk gathers take four rows per tensor-map gather
+  int32_t group_bytes;     // staging bytes per group of four rows (gather4: 128-byte multiple)
   int32_t cp_bytes;        // cp.async piece size when not using bulk copies (4, 8, 16)
   int32_t pre_bytes;       // bytes of the padded prefix array
   int64_t num_tiles;
@@ -234,9 +240,11 @@ __device__ __forceinline__ void cp_async(uint32_t saddr, const void* g, int byte
 // Store staged rows (row r at r * spitch vectors) to out rows j0 + r.
 // Rows of >= 32 vectors: one flat lane-strided walk (coalesced stores);
 // shorter rows: each lane stores its own row.
+// Staged row r sits at group r / 4 (gpitch vectors apart), row r % 4 of the
+// group (spitch vectors apart).
 template <int VEC>
 __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stage, int spitch,
-                                           int64_t j0, int rn, int lane) {
+                                           int gpitch, int64_t j0, int rn, int lane) {
   using V = typename VecT<VEC>::T;
   const int nvec = a.nvec;
   const V* sv = reinterpret_cast<const V*>(stage);
@@ -246,7 +254,7 @@ __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stag
     const int pieces = rn * nvec;
     int r = 0, c = lane;
     for (int p = lane; p < pieces; p += 32) {
-      dst[r * dstride + c] = sv[r * spitch + c];
+      dst[r * dstride + c] = sv[(r >> 2) * gpitch + (r & 3) * spitch + c];
       c += 32;
       if (c >= nvec) {
         c -= nvec;
@@ -254,27 +262,45 @@ __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stag
       }
     }
   } else if (lane < rn) {
-    for (int c = 0; c < nvec; ++c) dst[lane * dstride + c] = sv[lane * spitch + c];
+    const V* src = sv + (lane >> 2) * gpitch + (lane & 3) * spitch;
+    for (int c = 0; c < nvec; ++c) dst[lane * dstride + c] = src[c];
   }
 }
 
-// Issue the copies of rows s_idx[r0 .. r0+rn) into the warp's tile: one
-// Tensor Memory Accelerator bulk copy per lane (16-byte aligned rows), or
-// one cp.async chain per lane (any 4-byte alignment; lower latency when an SM
-// has only a few rows to fetch).
+// Issue the copies of rows s_idx[r0 .. r0+rn) into the warp's tile (row r
+// at group r / 4, row r % 4 of the group): one Tensor Memory Accelerator
+// gather of four rows per lane (`g4`: 16-byte aligned rows of at most 256
+// words, a 128-byte aligned tile; the issue cost per copy instruction, not
+// the bytes, bounds an SM's gather rate, so four rows per instruction), one
+// bulk copy per lane (16-byte aligned rows), or one cp.async chain per lane
+// (any 4-byte alignment; lower latency when an SM has only a few rows).
 __device__ __forceinline__ void gather_issue(const SampleArgs& a, unsigned char* stage,
                                              const int32_t* s_idx, int r0, int rn, int lane,
-                                             uint64_t* mbar) {
-  if (a.use_bulk) {
+                                             uint64_t* mbar, bool g4, const void* tmap) {
+  if (g4) {
+    const int ng = (rn + 3) >> 2;
+    per_fence_proxy_async_smem();  // earlier generic accesses of the tile before the copies
+    __syncwarp();
+    if (lane == 0) per_mbar_arrive_expect_tx(mbar, (uint32_t)(ng * 4 * a.row_bytes));
+    __syncwarp();
+    if (lane < ng) {  // a short last group repeats its last row
+      const int b = r0 + 4 * lane, last = r0 + rn - 1;
+      per_tma_gather4(stage + lane * a.group_bytes, tmap, 0, s_idx[b], s_idx[min(b + 1, last)],
+                      s_idx[min(b + 2, last)], s_idx[min(b + 3, last)], mbar);
+    }
+  } else if (a.use_bulk) {
     const float* row = a.t.storage + (int64_t)s_idx[r0 + min(lane, rn - 1)] * a.t.row_stride;
     per_fence_proxy_async_smem();  // earlier generic accesses of the tile before the bulk writes
     __syncwarp();
     if (lane == 0) per_mbar_arrive_expect_tx(mbar, (uint32_t)(rn * a.row_bytes));
     __syncwarp();
-    if (lane < rn) per_bulk_load(stage + lane * a.row_bytes, row, (uint32_t)a.row_bytes, mbar);
+    if (lane < rn)
+      per_bulk_load(stage + (lane >> 2) * a.group_bytes + (lane & 3) * a.row_bytes, row,
+                    (uint32_t)a.row_bytes, mbar);
   } else if (lane < rn) {
     const float* row = a.t.storage + (int64_t)s_idx[r0 + lane] * a.t.row_stride;
-    const uint32_t dst = per_smem_addr(stage + lane * a.row_bytes);
+    const uint32_t dst =
+        per_smem_addr(stage + (lane >> 2) * a.group_bytes + (lane & 3) * a.row_bytes);
     const int cpb = a.cp_bytes;
     const int pieces = a.row_bytes / cpb;
     const char* src = reinterpret_cast<const char*>(row);
@@ -294,7 +320,7 @@ __device__ __forceinline__ void gather_finish(const SampleArgs& a, unsigned char
     per_cp_async_wait_all();
   }
   __syncwarp();
-  store_rows<VEC>(a, stage, a.row_bytes / (VEC * 4), j0, rn, lane);
+  store_rows<VEC>(a, stage, a.row_bytes / (VEC * 4), a.group_bytes / (VEC * 4), j0, rn, lane);
   __syncwarp();
 }
 
@@ -322,8 +348,9 @@ constexpr int kSliceMax = 1024;  // owned-only routing: global draws per CTA
 constexpr int kAllToAllCtas = 64;  // max exchange: every CTA reads every slot up to this grid
 
 template <int VEC, bool SHARDED>
-__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(SampleArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2)
+    per_sample_kernel(SampleArgs a, const __grid_constant__ CUtensorMap rows_map) {
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double s_wsum[kMaxWarps + 1];
   __shared__ int32_t s_rows[kMaxWarps][32];
   __shared__ uint64_t s_mbar[kMaxWarps];
@@ -353,6 +380,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
   const int n_top = (int)t.level_len[top];
   double* s_pre = reinterpret_cast<double*>(smem);  // padded [n_top + 1]
   unsigned char* stage = smem + a.pre_bytes + (helper ? 0 : warp) * a.stage_bytes;
+  // four-row tensor gathers need 128-byte aligned tiles (pre_bytes and
+  // stage_bytes are multiples of 128); otherwise one bulk copy per row
+  const bool g4 = a.gather4 && (per_smem_addr(smem) & 127u) == 0u;
   uint32_t phase = 0u;
   if (!helper && a.use_bulk && lane == 0) {
     per_mbar_init(&s_mbar[warp], 1);
@@ -844,7 +874,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     }
     __syncwarp();
     const int rps = a.rows_per_stage;
-    if (rps > 0 && nrows > 0) gather_issue(a, stage, s_rows[warp], 0, min(rps, nrows), lane, &s_mbar[warp]);
+    if (rps > 0 && nrows > 0)
+      gather_issue(a, stage, s_rows[warp], 0, min(rps, nrows), lane, &s_mbar[warp], g4, &rows_map);
 
     float wv = 0.f;
     if (own) {
@@ -881,7 +912,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2) per_sample_kernel(Sam
     if (rps > 0) {
       for (int r0 = 0; r0 < nrows; r0 += rps) {
         const int rn = min(rps, nrows - r0);
-        if (r0 > 0) gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp]);
+        if (r0 > 0) gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp], g4, &rows_map);
         gather_finish<VEC>(a, stage, row0 + r0, rn, lane, &s_mbar[warp], phase);
       }
     }  // rows wider than a stage: copied by per_gather_rows_kernel after this kernel
@@ -982,6 +1013,78 @@ int owned_slice(int c, int world) {
   return best;
 }
 
+// Four-row tensor gathers of the rows (for every batch size: measured faster
+// than cp.async chains at a few rows per SM and than one bulk copy per row
+// at many); PER_GATHER4=0 turns them off.
+bool gather4_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("PER_GATHER4");
+    v = (s && s[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Tensor maps of row storages (2-D: row_stride words wide, capacity rows,
+// a box of one row of `box` words), built once per storage geometry.
+struct MapKey {
+  const float* storage;
+  int64_t row_stride;
+  int64_t capacity;
+  int box;
+  bool operator==(const MapKey& o) const {
+    return storage == o.storage && row_stride == o.row_stride && capacity == o.capacity &&
+           box == o.box;
+  }
+};
+constexpr int kMapSlots = 16;
+MapKey g_map_key[kMapSlots];
+CUtensorMap g_map[kMapSlots];
+int g_map_used = 0, g_map_next = 0;
+std::mutex g_map_mu;
+
+bool rows_map(const PerTree& t, int box, CUtensorMap* out) {
+  const MapKey k{t.storage, t.row_stride, t.capacity, box};
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  for (int i = 0; i < g_map_used; ++i)
+    if (g_map_key[i] == k) {
+      *out = g_map[i];
+      return true;
+    }
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    looked_up = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    else
+      cudaGetLastError();  // leave no sticky error behind
+  }
+  if (!encode || t.capacity < 1 || t.capacity > ((int64_t)1 << 31) || box < 4 || box > 256 ||
+      box > t.row_stride || (t.row_stride * 4) % 16 || ((uintptr_t)t.storage) % 16)
+    return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)t.row_stride, (cuuint64_t)t.capacity};
+  const cuuint64_t strides[1] = {(cuuint64_t)t.row_stride * 4};
+  const cuuint32_t boxdim[2] = {(cuuint32_t)box, 1};
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMap m;
+  if (encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)t.storage, dims, strides, boxdim, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  const int i = g_map_next;
+  g_map_next = (g_map_next + 1) % kMapSlots;
+  if (g_map_used < kMapSlots) ++g_map_used;
+  g_map_key[i] = k;
+  g_map[i] = m;
+  *out = m;
+  return true;
+}
+
 template <int VEC, bool SHARDED>
 int launch_vec(SampleArgs a, cudaStream_t stream) {
   const void* fn = (const void*)per_sample_kernel<VEC, SHARDED>;
@@ -989,7 +1092,7 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return per_record_cuda(e);
   const int n_top = (int)a.t.level_len[a.t.top_level];
-  a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 15) & ~15;
+  a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 127) & ~127;
   if (a.world <= 1) a.owned_only = 0;  // one shard owns every draw: no routing pass
   const int64_t warp_tiles = (a.batch + 31) / 32;
   // the shape chosen for this kernel, batch, world and store geometry is cached
@@ -1053,10 +1156,16 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     shape_store(key, sh);
   }
   const int64_t nw = sh.nw;
-  // a few rows per SM: cp.async has the lower latency; many: bulk copies
-  // keep more rows in flight
+  // without four-row gathers: a few rows per SM take cp.async chains (lower
+  // latency), many take bulk copies (more rows in flight)
   const int64_t busy_tiles = a.owned_only ? (warp_tiles + a.world - 1) / a.world : warp_tiles;
-  if (a.use_bulk && busy_tiles <= sh.sms) a.use_bulk = 0;
+  CUtensorMap tmap;  // the rows' tensor map when four-row gathers are on
+  memset(&tmap, 0, sizeof(tmap));
+  if (a.gather4 && !rows_map(a.t, a.row_bytes / 4, &tmap)) a.gather4 = 0;
+  if (!a.gather4) {
+    a.group_bytes = 4 * a.row_bytes;  // rows back to back in the tile
+    if (a.use_bulk && busy_tiles <= sh.sms) a.use_bulk = 0;
+  }
   const int threads = (int)(nw + 1) * 32;
   const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
   a.num_tiles = (a.batch + nw * 32 - 1) / (nw * 32);
@@ -1070,7 +1179,7 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     if (grid < 1) grid = 1;
     if (a.p2p && a.num_tiles > grid) return PER_ERR_TOO_LARGE;  // one tile per warp
   }
-  void* args[] = {&a};
+  void* args[] = {&a, &tmap};
   e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, grid > 1);
   return e == cudaSuccess ? PER_OK : per_record_cuda(e);
 }
@@ -1081,7 +1190,7 @@ template <int VEC>
 int max_wave_vec(SampleArgs a, int64_t* out) {
   const void* fn = (const void*)per_sample_kernel<VEC, true>;
   const int n_top = (int)a.t.level_len[a.t.top_level];
-  a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 15) & ~15;
+  a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 127) & ~127;
   const size_t smem = (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes;
   int rc = per_set_smem(fn, smem);
   if (rc) return rc;
@@ -1137,7 +1246,15 @@ void fill_common(SampleArgs& a, const PerTree& t, const float* rand, int64_t bat
   a.cp_bytes = cpb;
   a.use_bulk = (cpb == 16) ? 1 : 0;
   a.row_bytes = (int32_t)row_bytes;
-  if (row_bytes <= kStageMax) {
+  // four-row gathers: rows of at most 256 words, groups padded to 128 bytes
+  a.gather4 = (a.use_bulk && row_bytes <= 1024 && gather4_enabled()) ? 1 : 0;
+  a.group_bytes = (int32_t)(4 * row_bytes);
+  if (a.gather4) {
+    a.group_bytes = (int32_t)((4 * row_bytes + 127) & ~127ll);
+    const int groups = kStageMax / a.group_bytes < 8 ? kStageMax / a.group_bytes : 8;
+    a.stage_bytes = groups * a.group_bytes;
+    a.rows_per_stage = 4 * groups;
+  } else if (row_bytes <= kStageMax) {
     const int64_t want = 32 * row_bytes;
     a.stage_bytes = (int32_t)(want < kStageMax ? want : (kStageMax / row_bytes) * row_bytes);
     a.rows_per_stage = (int32_t)(a.stage_bytes / row_bytes);
@@ -1147,7 +1264,7 @@ void fill_common(SampleArgs& a, const PerTree& t, const float* rand, int64_t bat
     a.use_bulk = 0;
   }
   if (a.stage_bytes < kStageMin) a.stage_bytes = kStageMin;  // the level tiles share it
-  a.stage_bytes = (a.stage_bytes + 15) & ~15;
+  a.stage_bytes = (a.stage_bytes + 127) & ~127;  // tiles stay 128-byte aligned
 }
 
 // widest vector that every row start and both bases allow
