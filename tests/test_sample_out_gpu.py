@@ -84,3 +84,15 @@ def test_out_of_another_shape_is_rejected():
         a.sample_out(64, rows=torch.empty(64, a.row_dim, device="cuda")[:, :-1])
     with pytest.raises(ValueError):
         a.sample_out(64, idx=torch.empty(64, dtype=torch.int32, device="cuda"))
+
+
+def test_out_through_the_ctypes_path():
+    """The out= form without the torch binding (C ABI through ctypes)."""
+    a, b = _pair(cap=80_000)
+    b._engine = None
+    so = b.sample_out(512)
+    fa, ia, wa = a.sample(512, 0.4)
+    fb, ib, wb = b.sample(512, 0.4, out=so)
+    assert torch.equal(ia, ib) and torch.equal(wa, wb)
+    for k in fa:
+        assert torch.equal(fa[k], fb[k])
