@@ -219,6 +219,18 @@ __global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a
   if (threadIdx.x < kLMaxT) s_cnt[threadIdx.x] = 0;
   if (threadIdx.x == 0) s_max = 0u;
   per_wait_previous_grid();
+  // the first pass's entries are loaded together with the device count (a
+  // sharded update reads how many entries its sample owns): entries past the
+  // count are loaded (inside the caller's n) but not used
+  int64_t li[kLPer];
+  float tdv[kLPer];
+#pragma unroll
+  for (int q = 0; q < kLPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    const bool in = e < a.n && e < ncap;
+    li[q] = in ? slot_of(a, e) : -1;
+    tdv[q] = in ? a.td[e] : 0.f;
+  }
   const int64_t n = entries_of(a);
 
   // passes of `ncap` entries in order; a later pass overwrites an earlier
@@ -235,13 +247,16 @@ __global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a
       if (threadIdx.x == 0) s_max = 0u;
     }
     const int64_t c1 = min(c0 + ncap, n);
-    int64_t li[kLPer];
-    float tdv[kLPer];
 #pragma unroll
     for (int q = 0; q < kLPer; ++q) {
       const int64_t e = c0 + threadIdx.x + q * kThreads;
-      li[q] = e < c1 ? slot_of(a, e) : -1;
-      tdv[q] = e < c1 ? a.td[e] : 0.f;
+      if (c0 > 0) {
+        li[q] = e < c1 ? slot_of(a, e) : -1;
+        tdv[q] = e < c1 ? a.td[e] : 0.f;
+      } else if (e >= c1) {  // loaded past the device count: not an entry
+        li[q] = -1;
+        tdv[q] = 0.f;
+      }
     }
     __syncthreads();
 
