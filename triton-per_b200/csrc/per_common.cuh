@@ -23,9 +23,8 @@
 struct PerScratch {
   uint32_t bar_count;    // arrivals at the current grid barrier
   uint32_t bar_gen;      // generation, bumped by the last arriver
-  uint32_t mx_count;     // unused (kept for the layout)
   uint32_t mx_gen;       // sample: launch generation, bumped once every CTA has published
-  uint32_t mx_bits[2];   // unused (kept for the layout)
+  uint32_t pad0[3];
   unsigned long long draws[2];  // sharded sample: owned-draw counter, by generation parity
   unsigned long long mx_result;      // sample, large grids: (generation + 1) << 32 | max bits
   unsigned long long mx_result_cnt;  // sample, large grids: (generation + 1) << 32 | owned draws
