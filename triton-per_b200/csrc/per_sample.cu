@@ -347,9 +347,10 @@ constexpr int kBarRouted = 3;  // compute warps: the CTA's owned draws are queue
 constexpr int kSliceMax = 1024;  // owned-only routing: global draws per CTA
 constexpr int kAllToAllCtas = 64;  // max exchange: every CTA reads every slot up to this grid
 
+// The sample kernel's body; two kernels below run it with different register
+// budgets.
 template <int VEC, bool SHARDED>
-__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2)
-    per_sample_kernel(SampleArgs a, const __grid_constant__ CUtensorMap rows_map) {
+__device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorMap& rows_map) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double s_wsum[kMaxWarps + 1];
   __shared__ int32_t s_rows[kMaxWarps][32];
@@ -951,6 +952,24 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2)
   }
 }
 
+// CTAs of up to kMaxWarps + 1 warps, two per SM: the register allocator
+// counts such a CTA as 10 warps, so two fit in 64 K registers at 96 per thread.
+template <int VEC, bool SHARDED>
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2)
+    per_sample_kernel(SampleArgs a, const __grid_constant__ CUtensorMap rows_map) {
+  sample_body<VEC, SHARDED>(a, rows_map);
+}
+
+// CTAs of up to kR112Warps warps (helper included), two per SM at 112
+// registers per thread (16 warps x 32 x 112 = 57,344): the same body without
+// the 96-register build's spills.
+constexpr int kR112Warps = 8;
+template <int VEC, bool SHARDED>
+__global__ void __maxnreg__(112)
+    per_sample_kernel_r112(SampleArgs a, const __grid_constant__ CUtensorMap rows_map) {
+  sample_body<VEC, SHARDED>(a, rows_map);
+}
+
 // Launch shapes already chosen, per device, kernel, batch and store geometry
 // (small; a miss recomputes and overwrites round-robin).
 struct ShapeKey {
@@ -1088,6 +1107,9 @@ bool rows_map(const PerTree& t, int box, CUtensorMap* out) {
 template <int VEC, bool SHARDED>
 int launch_vec(SampleArgs a, cudaStream_t stream) {
   const void* fn = (const void*)per_sample_kernel<VEC, SHARDED>;
+  const void* fn112 = (const void*)per_sample_kernel_r112<VEC, SHARDED>;
+  // c compute warps + the helper: the 112-register build where it fits
+  auto fn_for = [&](int64_t c) { return c + 1 <= kR112Warps ? fn112 : fn; };
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return per_record_cuda(e);
@@ -1104,12 +1126,14 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     if (e != cudaSuccess) return per_record_cuda(e);
     int rc = per_set_smem(fn, (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes);
     if (rc) return rc;
+    rc = per_set_smem(fn112, (size_t)a.pre_bytes + (size_t)(kR112Warps - 1) * a.stage_bytes);
+    if (rc) return rc;
     int64_t nw = kMaxWarps, best_cost = -1, best_grid = 0;
     int max_ctas = 0, best_slice = 0;
     for (int c = kMaxWarps; c >= 1; --c) {
       int cap = 0;
-      rc = per_coresident_ctas(fn, (c + 1) * 32, (size_t)a.pre_bytes + (size_t)c * a.stage_bytes,
-                               &cap);
+      rc = per_coresident_ctas(fn_for(c), (c + 1) * 32,
+                               (size_t)a.pre_bytes + (size_t)c * a.stage_bytes, &cap);
       if (rc) return rc;
       if (a.owned_only) {
         // owned-only: slices sized so that no warp gets two tiles; among the
@@ -1145,7 +1169,7 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     }
     if (a.owned_only && best_cost < 0) return PER_ERR_TOO_LARGE;  // no one-wave shape
     if (best_cost < 0) {
-      rc = per_coresident_ctas(fn, (int)(nw + 1) * 32,
+      rc = per_coresident_ctas(fn_for(nw), (int)(nw + 1) * 32,
                                (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes, &max_ctas);
       if (rc) return rc;
     }
@@ -1180,7 +1204,7 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     if (a.p2p && a.num_tiles > grid) return PER_ERR_TOO_LARGE;  // one tile per warp
   }
   void* args[] = {&a, &tmap};
-  e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, grid > 1);
+  e = per_launch(fn_for(nw), (unsigned)grid, threads, smem, stream, args, grid > 1);
   return e == cudaSuccess ? PER_OK : per_record_cuda(e);
 }
 
