@@ -2,8 +2,9 @@
  * per_oracle.c - TEST INFRASTRUCTURE ONLY.
  *
  * CPU restatement of triton-per's `torch` backend, the reference semantics of
- * the replay hot path. It is the checker for the CUDA engine and the timed
- * CPU baseline; nothing in the engine links or calls it.
+ * the replay hot path. The tests compare the CUDA engine against it and the
+ * benchmark times it as the CPU baseline; nothing in the engine links or
+ * calls it.
  *
  * Followed line by line (reference paths within its project):
  *   src/triton_per/buffer.py:96-105   _sample_torch: full-length cumsum,

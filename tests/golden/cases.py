@@ -1,7 +1,7 @@
 """Seeded inputs of the golden cases (numpy only, no reference import).
 
-Each case is a deterministic function of its seed, so the GPU box rebuilds the
-same inputs that make_golden.py fed to the reference here; every case also
+Each case is a deterministic function of its seed, so a machine without the
+reference rebuilds the same inputs that make_golden.py fed to the reference; every case also
 carries a SHA-256 of its inputs, stored in the fixture, to catch any drift.
 Shapes and value distributions follow the workloads the reference is measured
 on (config 1 of the CPU run: capacity 100,000, fields obs32/action8/reward1/
