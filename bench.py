@@ -776,14 +776,14 @@ def main():
     achieved = ab / (k_us * 1e-6) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic_from_profiles(),
-                "peak_source": peak_kind, "kernel": "per_sample_kernel",
+                "peak_source": peak_kind, "kernel": "per_sample_kernel_r112 (fused sample, 112-register build)",
                 "kernel_us": k_us, "algo_bytes_per_launch": ab, "batch": BATCH}
     # the same kernel at the large-batch end of the sweep (1M x 74, batch 65,536)
     k64 = kernel_time_us(buf, 65536, reps=10, launches=8)
     ab64 = algo_bytes(65536, ROW_DIM)
     a64 = ab64 / (k64 * 1e-6) / 1e9
     roofline_large = {"bound": "hbm", "achieved": a64, "peak": peak, "unit": "GB/s",
-                      "frac": a64 / peak, "peak_source": peak_kind, "kernel": "per_sample_kernel",
+                      "frac": a64 / peak, "peak_source": peak_kind, "kernel": "per_sample_kernel_r112 (fused sample, 112-register build)",
                       "traffic": traffic_from_profiles("traffic_bytes_per_launch_b65536"),
                       "kernel_us": k64, "algo_bytes_per_launch": ab64, "batch": 65536}
 
