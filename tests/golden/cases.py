@@ -160,6 +160,27 @@ def case_add_wrap(seed=8):
     return dict(capacity=cap, fields={"x": 3}, adds=adds, upd_idx=upd_idx, upd_td=upd_td)
 
 
+def case_sumtree(seed=12):
+    """The reference's CPU sum tree (baselines/cpu_sumtree.py) on cap 1000 (not a
+    power of two): add 700, update 300 with duplicates, sample 512; add 500
+    (wraps), update 400 with larger TD errors, sample 512."""
+    rng = np.random.default_rng(seed)
+    cap = 1000
+    adds = [rng.standard_normal((700, 3), dtype=np.float32),
+            rng.standard_normal((500, 3), dtype=np.float32)]
+    upd_idx = [dup_indices(rng, rng.integers(0, 700, 300), 0.1),
+               dup_indices(rng, rng.integers(0, cap, 400), 0.1)]
+    upd_td = [np.abs(rng.standard_normal(300)).astype(np.float32),
+              (np.abs(rng.standard_normal(400)) * 5).astype(np.float32)]
+    rand = [rng.random(512), rng.random(512)]
+    return dict(capacity=cap, fields={"x": 3}, adds=adds, upd_idx=upd_idx, upd_td=upd_td,
+                rand=rand, beta=0.4)
+
+
+def sumtree_inputs_digest(c) -> str:
+    return digest(*c["adds"], *c["upd_idx"], *c["upd_td"], *c["rand"])
+
+
 SAMPLE_CASES = {
     "config1": case_config1,
     "small": case_small,

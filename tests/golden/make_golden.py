@@ -1,11 +1,13 @@
 """Generate the golden fixtures by running the REFERENCE itself.
 
 Runs triton-per's own `PERBuffer(..., backend="torch", device="cpu")`
-(src/triton_per/buffer.py) on the seeded inputs of cases.py and stores its
-outputs as .npz files beside this script. Only runs where the reference
-source tree is available (pass its path or set TRITON_PER_SRC):
+(src/triton_per/buffer.py) and its CPU sum tree `CpuSumTreePER(device="cpu")`
+(src/triton_per/baselines/cpu_sumtree.py) on the seeded inputs of cases.py and
+stores their outputs as .npz files beside this script. Only runs where the
+reference source tree is available (pass the path of its src/ directory or
+set TRITON_PER_SRC):
 
-    python tests/golden/make_golden.py /root/reference/src
+    python tests/golden/make_golden.py <reference>/src
 
 torch runs single-threaded here so that duplicate-index assignments keep the
 last occurrence deterministically (with several threads, torch's CPU index_put
@@ -13,6 +15,10 @@ splits the index list across threads and the survivor is unspecified).
 The sample fixtures call the buffer's `_sample_torch(rand, beta)` with the
 stored uniforms and normalise `w / w.max()` exactly as `sample()` does
 (buffer.py:92), so that the uniforms are shared with the engine under test.
+The sum-tree fixture runs the reference's sample() unchanged except that its
+random source (np.random.random, cpu_sumtree.py:77) returns the case's stored
+uniforms for the duration of the call, so that the restatement under test can
+be fed the same draws.
 """
 
 from __future__ import annotations
@@ -92,6 +98,32 @@ def add_case(PERBuffer, BLOCK_P, c):
     return out
 
 
+def sumtree_case(src, c):
+    from triton_per.baselines.cpu_sumtree import CpuSumTreePER
+
+    buf = CpuSumTreePER(c["capacity"], c["fields"], device="cpu")
+    out = {}
+    for k in range(2):
+        buf.add({"x": torch.from_numpy(c["adds"][k])})
+        out[f"s{k}_tree_after_add"] = buf.tree.tree.copy()
+        buf.update_priorities(torch.from_numpy(c["upd_idx"][k]), torch.from_numpy(c["upd_td"][k]))
+        out[f"s{k}_tree"] = buf.tree.tree.copy()
+        out[f"s{k}_max_priority"] = np.float64(buf._max_priority)
+        out[f"s{k}_cursor_size"] = np.array([buf._cursor, buf.size], np.int64)
+        rand = c["rand"][k]
+        orig = np.random.random
+        np.random.random = lambda n, _r=rand: _r[:n].copy()
+        try:
+            views, idx, w = buf.sample(rand.size, c["beta"])
+        finally:
+            np.random.random = orig
+        out[f"s{k}_idx"] = idx.numpy()
+        out[f"s{k}_w"] = w.numpy()
+        out[f"s{k}_rows"] = views["x"].numpy().copy()
+    out["inputs_digest"] = np.array(cases.sumtree_inputs_digest(c))
+    return out
+
+
 def main():
     src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TRITON_PER_SRC")
     if not src:
@@ -103,6 +135,7 @@ def main():
     np.savez(os.path.join(HERE, "update_dups.npz"), **update_case(PERBuffer, BLOCK_P, cases.case_update_dups()))
     np.savez(os.path.join(HERE, "update_storm.npz"), **update_case(PERBuffer, BLOCK_P, cases.case_update_storm()))
     np.savez(os.path.join(HERE, "add_wrap.npz"), **add_case(PERBuffer, BLOCK_P, cases.case_add_wrap()))
+    np.savez(os.path.join(HERE, "sumtree_small.npz"), **sumtree_case(src, cases.case_sumtree()))
     print("golden fixtures written to", HERE)
 
 
