@@ -191,8 +191,11 @@ int per_add(const per_store_t* store, const per_field_t* fields,
  * NULL. Stores of more than PER_NOALLOC_MAX_CAPACITY slots are rejected with
  * PER_ERR_TOO_LARGE. The first call on a device resolves the array's device
  * address (cudaGetSymbolAddress, with that device current): make it before
- * any stream capture. Every call first clears, on `stream`, the words it uses;
- * calls that overlap on the GPU share the array and race: serialise them.
+ * any stream capture; after cudaDeviceReset() on that device the cached
+ * address is stale, so do not call it there again. Batches of up to 4096
+ * indices use none of the array; larger ones first clear, on `stream`, the
+ * words they use. Calls that overlap on the GPU share the array and race:
+ * serialise them.
  * Calls no cudaMalloc, cudaFree or allocating library routine. */
 #define PER_NOALLOC_MAX_CAPACITY 1048576
 #define PER_NOALLOC_SCRATCH_BYTES 4346368

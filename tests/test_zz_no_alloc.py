@@ -71,6 +71,35 @@ def test_noalloc_update_matches_regular_entry_point():
     assert st["errors"] == 0 and st["timeouts"] == 0
 
 
+def test_noalloc_update_at_the_capacity_limit():
+    """A store of exactly PER_NOALLOC_MAX_CAPACITY slots fills the array's
+    claim regions to their computed bounds: a grid-path batch there gives the
+    regular entry point's tree."""
+    rng = np.random.default_rng(43)
+    cap = _lib.NOALLOC_MAX_CAPACITY
+    leaves = cases.leaves_abs_normal(rng, cap)
+    a = make_buffer(cap, {"x": 1}, None, leaves)
+    b = make_buffer(cap, {"x": 1}, None, leaves)
+    sb = _store_without_scratch(b)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for n in (8192, 5000):
+        idx, td = _batch(rng, cap, n)
+        idx[:2] = torch.tensor([0, cap - 1])  # the first and the last slot
+        rc_a = _lib.lib.per_update_priorities(a._store_ref, idx.data_ptr(), td.data_ptr(), n, stream)
+        rc_b = _lib.lib.per_update_priorities_noalloc(ctypes.byref(sb), idx.data_ptr(),
+                                                      td.data_ptr(), n, stream)
+        torch.cuda.synchronize()
+        assert rc_a == 0 and rc_b == 0, (rc_a, rc_b)
+        np.testing.assert_allclose(b.priorities.cpu().numpy(), a.priorities.cpu().numpy(),
+                                   rtol=1e-6, atol=0)
+        for k in range(1, a.num_levels):
+            np.testing.assert_allclose(b.level(k).cpu().numpy(), a.level(k).cpu().numpy(),
+                                       rtol=SUM_RTOL, atol=0)
+    check_tree(b)
+    st = b.status()
+    assert st["errors"] == 0 and st["timeouts"] == 0
+
+
 def test_noalloc_rejects_stores_larger_than_its_scratch():
     cap = _lib.NOALLOC_MAX_CAPACITY + 1
     buf = make_buffer(cap, {"x": 1})

@@ -62,7 +62,9 @@ bool pdl_enabled() {
   return v == 1;
 }
 
-PerTree tree_of(const per_store_t* s) {
+}  // namespace
+
+PerTree per_tree_of(const per_store_t* s) {
   PerTree t;
   for (int k = 0; k < PER_MAX_LEVELS; ++k) {
     t.levels[k] = s->levels[k];
@@ -86,28 +88,38 @@ PerTree tree_of(const per_store_t* s) {
   return t;
 }
 
-// Checks that a store descriptor is self-consistent with per_layout().
-int check_store(const per_store_t* s) {
+int per_check_store(const per_store_t* s, bool with_scratch) {
   if (!s) return PER_ERR_NULL_POINTER;
   per_layout_t l;
   int rc = per_layout(s->capacity, &l);
   if (rc) return rc;
   if (s->num_levels != l.num_levels || s->top_level != l.top_level) return PER_ERR_INVALID_ARGUMENT;
   for (int k = 0; k < l.num_levels; ++k) {
-    if (!s->levels[k] || !s->claims[k]) return PER_ERR_NULL_POINTER;
+    if (!s->levels[k] || (with_scratch && !s->claims[k])) return PER_ERR_NULL_POINTER;
     if (s->level_len[k] != l.level_len[k]) return PER_ERR_INVALID_ARGUMENT;
     if (((uintptr_t)s->levels[k]) % 16) return PER_ERR_MISALIGNED;
   }
-  if (!s->storage || !s->size_cursor || !s->max_priority || !s->status || !s->scratch)
+  if (!s->storage || !s->size_cursor || !s->max_priority || !s->status)
     return PER_ERR_NULL_POINTER;
-  if (s->scratch_bytes < PER_SCRATCH_BYTES) return PER_ERR_INVALID_ARGUMENT;
-  if (((uintptr_t)s->scratch) % 16 || ((uintptr_t)s->storage) % 4) return PER_ERR_MISALIGNED;
+  if (with_scratch) {
+    if (!s->scratch) return PER_ERR_NULL_POINTER;
+    if (s->scratch_bytes < PER_SCRATCH_BYTES) return PER_ERR_INVALID_ARGUMENT;
+    if (((uintptr_t)s->scratch) % 16) return PER_ERR_MISALIGNED;
+  }
+  if (((uintptr_t)s->storage) % 4) return PER_ERR_MISALIGNED;
   if (s->row_dim < 1 || s->row_stride < s->row_dim) return PER_ERR_INVALID_ARGUMENT;
   if (!(s->eps >= 0.f) || !(s->alpha == s->alpha)) return PER_ERR_INVALID_ARGUMENT;
   if (s->elem_bytes != 0 && s->elem_bytes != 4 && s->elem_bytes != 2) return PER_ERR_INVALID_ARGUMENT;
   if (s->elem_bytes == 2 && (s->row_dim % 2 || s->row_stride % 2)) return PER_ERR_INVALID_ARGUMENT;
   return PER_OK;
 }
+
+namespace {
+
+PerTree tree_of(const per_store_t* s) { return per_tree_of(s); }
+
+// Checks that a store descriptor is self-consistent with per_layout().
+int check_store(const per_store_t* s) { return per_check_store(s, true); }
 
 // out_stride (elements of the store) in the kernels' 4-byte words; -1 if a
 // 16-bit store gets an odd stride

@@ -292,6 +292,7 @@ __device__ __forceinline__ float per_sum32_tree(const float* c) {
   return __double2float_rn(p[0] + p[1]);
 }
 
+
 constexpr int PER_LINE_STRIDE = 144;                       // staged 128-byte line + 16 (no bank conflicts)
 constexpr int PER_NODE_LINES = 32 * PER_LINE_STRIDE;       // 32 staged lines
 constexpr int PER_NODE_TILE = PER_NODE_LINES + 32 * 8;     // + the warp's node list

@@ -9,6 +9,14 @@
 // Record a CUDA error for per_last_cuda_error() and return PER_ERR_CUDA.
 int per_record_cuda(cudaError_t e);
 
+// The kernels' view of a store descriptor (16-bit rows as 4-byte words).
+PerTree per_tree_of(const per_store_t* s);
+
+// PER_OK if the descriptor is self-consistent with per_layout(); with
+// with_scratch false, claims[] and scratch are not required (the caller
+// supplies its own).
+int per_check_store(const per_store_t* s, bool with_scratch);
+
 // Largest grid of `fn` (threads per CTA, dynamic shared bytes) whose CTAs are
 // all co-resident on the current device; cached per (device, fn, smem).
 int per_coresident_ctas(const void* fn, int threads, size_t smem, int* out);
@@ -38,6 +46,9 @@ int per_launch_sample(const PerTree& t, const float* rand, const PerRng* rng, in
                       cudaStream_t stream);
 int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int64_t n,
                       cudaStream_t stream);
+// True when per_launch_update() of n entries takes the grid path (claim words
+// and grid-barrier scratch); false for the single-CTA path, which uses neither.
+bool per_update_uses_grid(const PerTree& t, int64_t n);
 // Update with global indices: slot = idx - base; indices outside the store
 // are errors when strict, else skipped and counted as another shard's.
 int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, const int64_t* idx,

@@ -22,10 +22,14 @@
 // device current, resolves the address with cudaGetSymbolAddress and caches
 // it. Make that first call before any stream capture.
 //
-// All calls share the one array and it keeps the previous call's contents,
-// so every call first clears, on its stream, the claim words and barrier words
-// it will use. Two calls whose work overlaps on the GPU (different streams,
+// All calls share the one array and it keeps the previous call's contents.
+// Batches of up to 4096 indices take the single-CTA path, which uses none of
+// it; a larger batch first clears, on its stream, the claim words and barrier
+// words that its grid uses (a grid that gave up at a bounded wait may have
+// left them set). Two calls whose work overlaps on the GPU (different streams,
 // or different stores at the same time) race on the array: serialise them.
+// The cached address belongs to the device's current context: after
+// cudaDeviceReset() on a device, do not call this function there again.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -81,20 +85,9 @@ extern "C" int per_update_priorities_noalloc(const per_store_t* s, const int64_t
                                              const float* td, int64_t n, void* stream) {
   if (!s) return PER_ERR_NULL_POINTER;
   if (s->capacity > PER_NOALLOC_MAX_CAPACITY) return PER_ERR_TOO_LARGE;
-  per_layout_t l;
-  int rc = per_layout(s->capacity, &l);
+  int rc = per_check_store(s, false);  // claims[] and scratch come from the array
   if (rc) return rc;
-  if (s->num_levels != l.num_levels || s->top_level != l.top_level || l.num_levels != 3)
-    return PER_ERR_INVALID_ARGUMENT;
-  for (int k = 0; k < l.num_levels; ++k) {
-    if (!s->levels[k]) return PER_ERR_NULL_POINTER;
-    if (s->level_len[k] != l.level_len[k]) return PER_ERR_INVALID_ARGUMENT;
-    if (((uintptr_t)s->levels[k]) % 16) return PER_ERR_MISALIGNED;
-  }
-  if (!s->storage || !s->size_cursor || !s->max_priority || !s->status)
-    return PER_ERR_NULL_POINTER;
-  if (s->row_dim < 1 || s->row_stride < s->row_dim) return PER_ERR_INVALID_ARGUMENT;
-  if (!(s->eps >= 0.f) || !(s->alpha == s->alpha)) return PER_ERR_INVALID_ARGUMENT;
+  if (s->num_levels != 3) return PER_ERR_INVALID_ARGUMENT;
   if (!idx || !td) return PER_ERR_NULL_POINTER;
   if (n < 1) return PER_ERR_EMPTY;
   if (n >= (int64_t)0xffffffffLL) return PER_ERR_TOO_LARGE;
@@ -103,33 +96,21 @@ extern "C" int per_update_priorities_noalloc(const per_store_t* s, const int64_t
   rc = scratch_address(&base);
   if (rc) return rc;
 
-  PerTree t;
-  for (int k = 0; k < PER_MAX_LEVELS; ++k) {
-    t.levels[k] = s->levels[k];
-    t.claims[k] = nullptr;
-    t.level_len[k] = s->level_len[k];
-  }
+  PerTree t = per_tree_of(s);
+  for (int k = 0; k < PER_MAX_LEVELS; ++k) t.claims[k] = nullptr;
   t.claims[0] = reinterpret_cast<uint32_t*>(base + kOffClaims0);
   t.claims[1] = reinterpret_cast<uint32_t*>(base + kOffClaims1);
   t.claims[2] = reinterpret_cast<uint32_t*>(base + kOffClaims2);
-  t.num_levels = s->num_levels;
-  t.top_level = s->top_level;
-  t.capacity = s->capacity;
-  t.storage = s->storage;
-  t.row_dim = s->row_dim;
-  t.row_stride = s->row_stride;
-  t.size_cursor = s->size_cursor;
-  t.max_priority = s->max_priority;
-  t.status = s->status;
   t.scratch = reinterpret_cast<PerScratch*>(base + kOffBarrier);
-  t.alpha = s->alpha;
-  t.eps = s->eps;
 
-  // the previous call's contents stay in the array: clear what must start at zero
+  // the single-CTA path touches none of the array; the grid path starts from
+  // cleared barrier and claim words (the previous call's contents stay)
   cudaStream_t st = (cudaStream_t)stream;
-  cudaError_t e = cudaMemsetAsync(base + kOffBarrier, 0, PER_SCRATCH_BYTES, st);
-  for (int k = 0; k < 3 && e == cudaSuccess; ++k)
-    e = cudaMemsetAsync(t.claims[k], 0, (size_t)l.level_len[k] * 4, st);
-  if (e != cudaSuccess) return per_record_cuda(e);
+  if (per_update_uses_grid(t, n)) {
+    cudaError_t e = cudaMemsetAsync(base + kOffBarrier, 0, PER_SCRATCH_BYTES, st);
+    for (int k = 0; k < 3 && e == cudaSuccess; ++k)
+      e = cudaMemsetAsync(t.claims[k], 0, (size_t)s->level_len[k] * 4, st);
+    if (e != cudaSuccess) return per_record_cuda(e);
+  }
   return per_launch_update(t, idx, td, n, st);
 }

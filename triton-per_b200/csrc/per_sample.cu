@@ -70,7 +70,10 @@ struct SampleArgs {
   int32_t gather4;         // bulk gathers take four rows per tensor-map gather
   int32_t group_bytes;     // staging bytes per group of four rows (gather4: 128-byte multiple)
   int32_t cp_bytes;        // cp.async piece size when not using bulk copies (4, 8, 16)
-  int32_t pre_bytes;       // bytes of the padded prefix array
+  int32_t pre_bytes;       // shared-memory bytes of the staged top level (128-byte multiple)
+  int32_t draws_per_warp;  // draws per warp and tile (32; fewer in wide mode)
+  int32_t wide;            // rows copied in this kernel piecewise by bulk copies (wide rows)
+  int32_t wide_piece;      // wide mode: bytes per piece and per lane of the warp's tile
   int64_t num_tiles;
   // sharded mode: this store is shard `rank` of `world` shards
   const double* stats;           // [world][2] of every shard: total priority, live size
@@ -213,6 +216,57 @@ __device__ __forceinline__ int search32(const float* c, double r, double* ex, fl
   return 4 * kq + j;
 }
 
+// The leaf level: only the child and its value are needed (no residual for
+// a level below). A float32 prefix of the 32 children decides whenever r lies
+// farther than a rounding margin from both ends of the chosen child's range;
+// otherwise (r within the margin of a boundary, at or past the node's sum, an
+// empty node) the exact float64 search32 decides. The float32 partial sums
+// take at most 12 additions of non-negative values, so each is within
+// 12 u S of its exact value (u = 2^-24, S = the children's sum), and
+// (float)r within u S of r; the margin is 64 u S, so the fast answer is the
+// exact one whenever it is taken.
+__device__ __forceinline__ int search32_leaf(const float* c, double r, float* val, bool* fb) {
+  float P[9];
+  P[0] = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) P[k + 1] = P[k] + ((c[4 * k] + c[4 * k + 1]) + (c[4 * k + 2] + c[4 * k + 3]));
+  const float rf = __double2float_rn(r);
+  const float M = P[8] * 3.814697265625e-06f;  // 64 * 2^-24
+  int kq = 8;
+#pragma unroll
+  for (int k = 7; k >= 0; --k)
+    if (P[k + 1] > rf) kq = k;
+  float base = 0.f, top = P[8], e0 = c[0], e1 = c[1], e2 = c[2];
+#pragma unroll
+  for (int k = 1; k < 8; ++k)
+    if (k == kq) {
+      base = P[k];
+      e0 = c[4 * k];
+      e1 = c[4 * k + 1];
+      e2 = c[4 * k + 2];
+    }
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    if (k == kq) top = P[k + 1];
+  const float s1 = base + e0, s2 = s1 + e1, s3 = s2 + e2;
+  const int j = s1 > rf ? 0 : s2 > rf ? 1 : s3 > rf ? 2 : 3;
+  const float lo = j == 0 ? base : j == 1 ? s1 : j == 2 ? s2 : s3;
+  const float hi = j == 0 ? s1 : j == 1 ? s2 : j == 2 ? s3 : top;
+  // the lower end of child 0 of quad 0 is exactly 0 <= r
+  const bool ok = kq < 8 && hi - rf > M && (kq == 0 && j == 0 ? true : rf - lo > M);
+  if (!ok) {
+    double ex;
+    return search32(c, r, &ex, val, fb);
+  }
+  const int f = 4 * kq + j;
+  float v = c[0];
+#pragma unroll
+  for (int i = 1; i < 32; ++i)
+    if (i == f) v = c[i];
+  *val = v;
+  return f;
+}
+
 template <int VEC>
 struct VecT;
 template <>
@@ -347,6 +401,117 @@ constexpr int kBarRouted = 3;  // compute warps: the CTA's owned draws are queue
 constexpr int kSliceMax = 1024;  // owned-only routing: global draws per CTA
 constexpr int kAllToAllCtas = 64;  // max exchange: every CTA reads every slot up to this grid
 
+// Poll the tagged slots of CTAs [0, n) of this launch until every one carries
+// `tag` (bounded): lane l takes slots l, l + 32, ... and each poll issues all
+// of a lane's pending loads before it looks at any of them, so one poll costs
+// one L2 round trip however many slots are pending. Returns the max of the
+// first words' data and the sum of the second words' data (sharded: the
+// owned-draw counts), reduced over the warp; false on timeout.
+template <bool SHARDED>
+__device__ __forceinline__ bool gather_slots(const unsigned long long* slots, int n, uint32_t tag,
+                                             int lane, uint32_t* mb_out,
+                                             unsigned long long* owned_out) {
+  constexpr int kChunk = 16;
+  static_assert(kMaxGrid / 32 <= 32, "one pending bit per slot of a lane");
+  uint32_t mb = 0u;
+  unsigned long long owned = 0ull;
+  const int nper = (n - lane + 31) / 32;  // slots of this lane
+  uint32_t pending = nper >= 32 ? 0xffffffffu : ((1u << nper) - 1u);
+  bool ok = true;
+  for (uint32_t it = 0; __any_sync(PER_FULL_MASK, pending != 0u); ++it) {
+    if (it > PER_SPIN_LIMIT) {
+      ok = false;
+      break;
+    }
+#pragma unroll
+    for (int c0 = 0; c0 < 32; c0 += kChunk) {
+      if (!__any_sync(PER_FULL_MASK, ((pending >> c0) & ((1u << kChunk) - 1u)) != 0u)) continue;
+      unsigned long long v[kChunk], m[kChunk];
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) {
+        const int c = lane + 32 * (c0 + i);
+        const bool p = (pending >> (c0 + i)) & 1u;
+        v[i] = p ? per_ld_relaxed_u64(slots + 2 * c) : 0ull;
+        m[i] = (SHARDED && p) ? per_ld_relaxed_u64(slots + 2 * c + 1) : 0ull;
+      }
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) {
+        const bool p = (pending >> (c0 + i)) & 1u;
+        if (p && (uint32_t)(v[i] >> 32) == tag && (!SHARDED || (uint32_t)(m[i] >> 32) == tag)) {
+          mb = max(mb, (uint32_t)v[i]);
+          owned += (uint32_t)m[i];
+          pending &= ~(1u << (c0 + i));
+        }
+      }
+    }
+    if (pending) __nanosleep(PER_SPIN_SLEEP_NS);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
+    owned += __shfl_xor_sync(PER_FULL_MASK, owned, o);
+  }
+  *mb_out = mb;
+  *owned_out = owned;
+  return ok;
+}
+
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+               "r"(per_smem_addr(ssrc)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// this thread's bulk stores have finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// this thread's bulk stores are complete
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Rows wider than a warp's staging tile (wide mode: 16-byte aligned rows and
+// output rows): lane l < nact copies storage row `slot` to output row `orow`
+// in pieces of a.wide_piece bytes through its own slot of the warp's tile, a
+// bulk load (completing on the warp's mbarrier) then a bulk store per piece.
+// The stores of the last piece may still be writing to the output when this
+// returns (the kernel waits for them before it exits).
+__device__ __forceinline__ void wide_copy(const SampleArgs& a, unsigned char* stage, int64_t slot,
+                                          int64_t orow, int lane, int nact, uint64_t* mbar,
+                                          uint32_t& phase) {
+  const int64_t rb = a.t.row_dim * 4;
+  const int64_t piece = a.wide_piece;
+  const bool act = lane < nact;
+  unsigned char* mine = stage + (int64_t)lane * piece;
+  const char* src = reinterpret_cast<const char*>(a.t.storage + slot * a.t.row_stride);
+  char* dst = reinterpret_cast<char*>(a.out + orow * a.out_stride);
+  for (int64_t off = 0; off < rb; off += piece) {
+    const uint32_t nb = (uint32_t)(rb - off < piece ? rb - off : piece);
+    if (act) bulk_wait_read();  // the slot's previous stores have read it
+    per_fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) per_mbar_arrive_expect_tx(mbar, nb * (uint32_t)nact);
+    __syncwarp();
+    if (act) per_bulk_load(mine, src + off, nb, mbar);
+    per_mbar_wait(mbar, phase, a.t.status);
+    phase ^= 1u;
+    if (act) {
+      bulk_store(dst + off, mine, nb);
+      bulk_commit();
+    }
+  }
+  // the tile is reused by the next tile's level lines: its stores must have
+  // read it (their writes to the output may still be in flight)
+  if (act) bulk_wait_read();
+  __syncwarp();
+}
+
 // The sample kernel's body; two kernels below run it with different register
 // budgets.
 template <int VEC, bool SHARDED>
@@ -374,7 +539,8 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   const int nthreads = blockDim.x;
   const int nwarps = (nthreads >> 5) - 1;  // compute warps; the last warp is the helper
   const bool helper = warp == nwarps;
-  const int64_t tile_draws = (int64_t)nwarps * 32;
+  const int D = a.draws_per_warp;  // draws per warp and tile: 32, fewer for wide rows
+  const int64_t tile_draws = (int64_t)nwarps * D;
   const PerTree& t = a.t;
   PerScratch* sc = t.scratch;
   const int top = t.top_level;
@@ -385,20 +551,19 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   // stage_bytes are multiples of 128); otherwise one bulk copy per row
   const bool g4 = a.gather4 && (per_smem_addr(smem) & 127u) == 0u;
   uint32_t phase = 0u;
-  if (!helper && a.use_bulk && lane == 0) {
+  if (!helper && (a.use_bulk || a.wide) && lane == 0) {
     per_mbar_init(&s_mbar[warp], 1);
     per_fence_mbar_init();
   }
   per_wait_previous_grid();
 
-  // early, independent loads: generation of the max exchange, size, first uniform
   const uint32_t gen = SHARDED || helper ? per_ld_relaxed_u32(&sc->mx_gen) : 0u;
   const int64_t size = __ldg(t.size_cursor);
   // every CTA reads the stream position before it arrives at the max exchange;
   // CTA 0 advances it after the exchange has completed
   const unsigned long long cbase = a.use_rng ? per_ld_relaxed_u64(a.rng_counter) : 0ull;
   int64_t tile = blockIdx.x;
-  float rnd0 = 0.f;
+  float rnd0 = 0.f;  // this lane's first uniform
   // sharded, in-kernel exchange: this rank's mailbox and the sequence number
   // of its last call (thread 0), and the peers' mailboxes (warp 0 of CTA 0,
   // which publishes the statistics), loaded during the prologue
@@ -453,8 +618,8 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
       loc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
     }
     // this lane's first uniform, while the scan below waits on shuffles
-    if (!helper && !(SHARDED && a.owned_only)) {
-      const int64_t j = tile * tile_draws + threadIdx.x;
+    if (!helper && !(SHARDED && a.owned_only) && lane < D) {
+      const int64_t j = tile * tile_draws + warp * D + lane;
       if (tile < a.num_tiles && j < a.batch) rnd0 = draw_uniform(a, cbase, j);
     }
     const double incl = per_warp_scan_incl(loc, lane);
@@ -565,38 +730,9 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
       if (SHARDED) per_st_relaxed_u64(&slots[2 * blockIdx.x + 1], ((unsigned long long)tag << 32) | s_cta_own);
     }
     if (gridDim.x <= kAllToAllCtas || blockIdx.x == 0) {
-      // small grids: every helper reads all slots; large grids: CTA 0 does,
-      // each lane polling its slots together (one round trip per poll)
-      constexpr int kPer = kMaxGrid / 32;
-      static_assert(kPer <= 64, "one pending bit per slot of a lane");
-      unsigned long long pending = 0ull;  // bit i: slot lane + 32 i not seen yet
-      for (int i = 0; i < kPer && lane + 32 * i < (int)gridDim.x; ++i) pending |= 1ull << i;
-      for (uint32_t it = 0; __any_sync(PER_FULL_MASK, pending != 0ull); ++it) {
-        if (it > PER_SPIN_LIMIT) {
-          timed_out = true;
-          break;
-        }
-        unsigned long long left = pending;
-        while (left) {
-          const int i = __ffsll((long long)left) - 1;
-          left &= left - 1;
-          const int c = lane + 32 * i;
-          const unsigned long long v = per_ld_relaxed_u64(&slots[2 * c]);
-          const unsigned long long n = SHARDED ? per_ld_relaxed_u64(&slots[2 * c + 1])
-                                               : ((unsigned long long)tag << 32);
-          if ((uint32_t)(v >> 32) == tag && (uint32_t)(n >> 32) == tag) {
-            mb = max(mb, (uint32_t)v);
-            owned += (uint32_t)n;
-            pending &= ~(1ull << i);
-          }
-        }
-        if (pending) __nanosleep(PER_SPIN_SLEEP_NS);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
-        owned += __shfl_xor_sync(PER_FULL_MASK, owned, o);
-      }
+      // small grids: every helper reads all slots; large grids: CTA 0 does
+      // and publishes two tagged totals
+      timed_out = !gather_slots<SHARDED>(slots, (int)gridDim.x, tag, lane, &mb, &owned);
       if (lane == 0 && blockIdx.x == 0) {  // all CTAs have read gen: next generation
         if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
         sc->mx_gen = gen + 1u;
@@ -744,9 +880,9 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
 
   for (; tile < ntiles; tile += tstep) {
     const bool last_tile = tile + tstep >= ntiles;
-    const int64_t wj0 = tile * tile_draws + warp * 32;  // first draw of this warp
+    const int64_t wj0 = tile * tile_draws + warp * D;  // first draw of this warp
     int64_t j = wj0 + lane;
-    bool ok = j < a.batch;
+    bool ok = lane < D && j < a.batch;
     if (owned_mode) {
       const int64_t k = tile * 32 + lane;
       ok = k < s_qn;
@@ -803,10 +939,14 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     r -= s_pre[ppos(k)];
     float p = 0.f;
 
-    // lower levels: stage each draw's 32 children, search them per lane
+    // lower levels: stage each draw's 32 children, search them per lane (the
+    // leaf level through the float32 fast path). Only lanes with a draw (lanes
+    // 0 .. nact-1) fetch lines: idle lanes would all walk toward slot 0 and
+    // pile onto one L2 line; their search reads stale lines and is discarded.
+    const int nact = __popc(__ballot_sync(PER_FULL_MASK, ok));
     for (int L = top - 1; L >= 0; --L) {
       __syncwarp();
-      per_stage_lines(t.levels[L], stage, 32, lane,
+      per_stage_lines(t.levels[L], stage, nact, lane,
                       [&](int d) { return __shfl_sync(PER_FULL_MASK, node, d); });
       const float4* my = reinterpret_cast<const float4*>(stage + lane * PER_LINE_STRIDE);
       float c[32];
@@ -818,9 +958,14 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
         c[4 * i + 2] = v.z;
         c[4 * i + 3] = v.w;
       }
-      double ex;
-      const int f = search32(c, r, &ex, &p, &fb);
-      r -= ex;
+      int f;
+      if (L == 0) {
+        f = search32_leaf(c, r, &p, &fb);
+      } else {
+        double ex;
+        f = search32(c, r, &ex, &p, &fb);
+        r -= ex;
+      }
       node = node * PER_FANOUT + f;
     }
 
@@ -871,7 +1016,7 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     } else {
       s_rows[warp][lane] = (int32_t)i;
       row0 = wj0;
-      nrows = (int)min((int64_t)32, a.batch - wj0);
+      nrows = (int)min((int64_t)D, a.batch - wj0);
     }
     __syncwarp();
     const int rps = a.rows_per_stage;
@@ -916,7 +1061,9 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
         if (r0 > 0) gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp], g4, &rows_map);
         gather_finish<VEC>(a, stage, row0 + r0, rn, lane, &s_mbar[warp], phase);
       }
-    }  // rows wider than a stage: copied by per_gather_rows_kernel after this kernel
+    } else if (!SHARDED && a.wide && nrows > 0) {
+      wide_copy(a, stage, i, j, lane, nrows, &s_mbar[warp], phase);
+    }  // other rows wider than a stage: per_gather_rows_kernel after this kernel
   }
 
   if (lane == 0) {
@@ -946,10 +1093,11 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   }
   const float gmax = s_gmax;
   for (int64_t tl = blockIdx.x; tl < a.num_tiles; tl += gridDim.x) {
-    const int64_t j = tl * tile_draws + warp * 32 + lane;
+    const int64_t j = tl * tile_draws + warp * D + lane;
     const bool last = tl + gridDim.x >= a.num_tiles;
-    if (j < a.batch) a.w[j] = __fdiv_rn(last ? w_last : a.w[j], gmax);
+    if (lane < D && j < a.batch) a.w[j] = __fdiv_rn(last ? w_last : a.w[j], gmax);
   }
+  if (a.wide) bulk_wait_all();  // the last row stores are complete before the CTA exits
 }
 
 // CTAs of up to kMaxWarps + 1 warps, two per SM: the register allocator
@@ -1104,6 +1252,60 @@ bool rows_map(const PerTree& t, int box, CUtensorMap* out) {
   return true;
 }
 
+// Shared-memory bytes of the padded float64 prefix of the top level
+// (n_top + 1 entries, one spare every 32), rounded up to 128 (the row tiles
+// behind it stay 128-byte aligned).
+int32_t top_bytes(const PerTree& t) {
+  const int n_top = (int)t.level_len[t.top_level];
+  return (int32_t)(((n_top + 1 + (n_top >> 5) + 1) * 8 + 127) & ~127);
+}
+
+// Wide mode (rows wider than a warp's staging tile): one CTA per SM, each
+// taking an equal share of the batch as nw compute warps (at most
+// kR112Warps - 1) of D draws; every lane stages its row in pieces that fill
+// the CTA's shared memory, right after its search (copies that start while
+// other CTAs still walk the tree measured faster than copies held back until
+// every walk is done).
+constexpr size_t kWideSmem = 200 * 1024;
+
+template <int VEC>
+int launch_wide(SampleArgs a, cudaStream_t stream) {
+  const void* fn = (const void*)per_sample_kernel_r112<VEC, false>;
+  int dev = 0, sms = 148;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return per_record_cuda(e);
+  const int64_t ctas = a.batch < sms ? a.batch : sms;
+  const int64_t per_cta = (a.batch + ctas - 1) / ctas;
+  const int nw = (int)(per_cta < kR112Warps - 1 ? per_cta : kR112Warps - 1);
+  int64_t D = (per_cta + nw - 1) / nw;
+  if (D > 32) D = 32;
+  const int64_t rb = a.t.row_dim * 4;
+  int64_t piece = ((int64_t)kWideSmem - a.pre_bytes) / (nw * D) / 16 * 16;
+  if (piece > rb) piece = rb;
+  if (piece < 16) return PER_ERR_TOO_LARGE;
+  a.draws_per_warp = (int32_t)D;
+  a.wide_piece = (int32_t)piece;
+  a.stage_bytes = (int32_t)((D * piece + 127) & ~127ll);
+  if (a.stage_bytes < kStageMin) a.stage_bytes = (kStageMin + 127) & ~127;
+  const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
+  int rc = per_set_smem(fn, smem);
+  if (rc) return rc;
+  const int threads = (nw + 1) * 32;
+  int max_ctas = 0;
+  rc = per_coresident_ctas(fn, threads, smem, &max_ctas);
+  if (rc) return rc;
+  a.num_tiles = (a.batch + nw * D - 1) / (nw * D);
+  int64_t grid = a.num_tiles < max_ctas ? a.num_tiles : max_ctas;
+  if (grid > kMaxGrid) grid = kMaxGrid;
+  if (grid < 1) grid = 1;
+  CUtensorMap tmap;  // unused in wide mode
+  memset(&tmap, 0, sizeof(tmap));
+  void* args[] = {&a, &tmap};
+  e = per_launch(fn, (unsigned)grid, threads, smem, stream, args, grid > 1);
+  return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+}
+
 template <int VEC, bool SHARDED>
 int launch_vec(SampleArgs a, cudaStream_t stream) {
   const void* fn = (const void*)per_sample_kernel<VEC, SHARDED>;
@@ -1113,8 +1315,6 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return per_record_cuda(e);
-  const int n_top = (int)a.t.level_len[a.t.top_level];
-  a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 127) & ~127;
   if (a.world <= 1) a.owned_only = 0;  // one shard owns every draw: no routing pass
   const int64_t warp_tiles = (a.batch + 31) / 32;
   // the shape chosen for this kernel, batch, world and store geometry is cached
@@ -1213,8 +1413,6 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
 template <int VEC>
 int max_wave_vec(SampleArgs a, int64_t* out) {
   const void* fn = (const void*)per_sample_kernel<VEC, true>;
-  const int n_top = (int)a.t.level_len[a.t.top_level];
-  a.pre_bytes = ((n_top + 1 + (n_top >> 5) + 1) * 8 + 127) & ~127;
   const size_t smem = (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes;
   int rc = per_set_smem(fn, smem);
   if (rc) return rc;
@@ -1241,7 +1439,10 @@ void fill_common(SampleArgs& a, const PerTree& t, const float* rand, int64_t bat
   a.idx = idx;
   a.w = w;
   a.num_tiles = 0;
-  a.pre_bytes = 0;
+  a.pre_bytes = top_bytes(t);
+  a.draws_per_warp = 32;
+  a.wide = 0;
+  a.wide_piece = 0;
   a.stats = nullptr;
   a.rank = 0;
   a.world = 1;
@@ -1374,6 +1575,16 @@ int launch_gather_rows(const SampleArgs& a, int vec, int64_t base, cudaStream_t 
 template <bool SHARDED>
 int launch_any(SampleArgs& a, int vec, cudaStream_t stream) {
   a.nvec = (int32_t)(a.t.row_dim / vec);
+  // rows wider than a stage: copied inside the sample kernel when rows and
+  // output rows are 16-byte aligned (bulk copies), else by
+  // per_gather_rows_kernel after it
+  if (!SHARDED && a.rows_per_stage == 0 && a.cp_bytes == 16 && (a.t.row_dim * 4) % 16 == 0 &&
+      ((uintptr_t)a.out) % 16 == 0 && (a.out_stride * 4) % 16 == 0) {
+    a.wide = 1;
+    return vec == 4   ? launch_wide<4>(a, stream)
+           : vec == 2 ? launch_wide<2>(a, stream)
+                      : launch_wide<1>(a, stream);
+  }
   int rc = vec == 4   ? launch_vec<4, SHARDED>(a, stream)
            : vec == 2 ? launch_vec<2, SHARDED>(a, stream)
                       : launch_vec<1, SHARDED>(a, stream);

@@ -192,7 +192,7 @@ __host__ __device__ __forceinline__ size_t lines_smem(int T, int ncap) {
          + (size_t)2 * T * ncap * 4;                 // node lists + parents' set slots
 }
 
-__global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a, int ncap) {
+__global__ void __launch_bounds__(kThreads, 1) per_update_lines_kernel(UpdateArgs a, int ncap) {
   const PerTree& t = a.t;
   const int T = t.num_levels - 1;
   extern __shared__ __align__(16) unsigned char s_dyn[];
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a
   uint32_t* pslot = list + T * ncap;       // [T][ncap] set slot of the node's parent
   __shared__ int s_cnt[kLMaxT];
   __shared__ uint32_t s_max;
-  __shared__ uint32_t s_fresh[kThreads / 32][32];  // list positions of a warp's new nodes
+  __shared__ uint32_t s_fresh[kThreads / 32][32];  // nodes a warp entered first, in list order
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const uint32_t lbase = per_smem_addr_generic(lines);
@@ -274,15 +274,19 @@ __global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a
       slot[q] = -1;
       lslot0[q] = -1;
       np[q] = 0.f;
+      // the same for every thread of the block: a pass past the last entry
+      // has nothing to elect (a batch of at most kThreads takes one)
+      if (c0 + (int64_t)q * kThreads >= c1) continue;
       bool valid = false;
       if (e < c1) {
         if (li[q] < 0 || li[q] >= t.capacity) {
           if (a.strict) ++nbad; else ++nforeign;
         } else {
           valid = true;
+          // the slot's table entry first: the atomics' round trips overlap powf
+          slot[q] = lset_insert(wkey, (uint32_t)li[q]);
           np[q] = new_priority(t, tdv[q]);
           tmax = max(tmax, __float_as_uint(np[q]));
-          slot[q] = lset_insert(wkey, (uint32_t)li[q]);
           if (slot[q] >= 0) atomicMax(&wval[slot[q]], (uint32_t)(e + 1));
         }
       }
@@ -316,17 +320,26 @@ __global__ void __launch_bounds__(kThreads) per_update_lines_kernel(UpdateArgs a
         if (fresh) {
           list[L * ncap + newp] = nd;
           spos[L * kLHash + sl] = (uint32_t)newp;
-          s_fresh[warp][newp - pbase] = (uint32_t)newp;
+          s_fresh[warp][newp - pbase] = nd;  // the node of the warp's (newp - pbase)-th new entry
         }
         __syncwarp();
         // the warp fetches its new nodes' lines together, 4 lines (8 x 16 B
-        // each) per instruction
+        // each) per instruction: every node index is read first, then all
+        // the copies go out back to back
         const float* clevel = t.levels[L];
-        for (int g = lane >> 3; g < nf; g += 4) {
-          const int p = (int)s_fresh[warp][g];
-          const int part = lane & 7;
-          per_cp_async16(lbase + (uint32_t)((L * ncap + p) * PER_LINE_STRIDE + part * 16),
-                         clevel + (int64_t)list[L * ncap + p] * PER_FANOUT + part * 4);
+        const int part = lane & 7;
+        uint32_t gn[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int g = (lane >> 3) + 4 * i;
+          gn[i] = g < nf ? s_fresh[warp][g] : 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int g = (lane >> 3) + 4 * i;
+          if (g < nf)
+            per_cp_async16(lbase + (uint32_t)((L * ncap + pbase + g) * PER_LINE_STRIDE + part * 16),
+                           clevel + (int64_t)gn[i] * PER_FANOUT + part * 4);
         }
         __syncwarp();
         below_p = newp;
@@ -503,6 +516,26 @@ int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int
   return per_launch_update_shard(t, 0, 1, idx, td, n, nullptr, stream);
 }
 
+namespace {
+
+// Entries per pass of the single-CTA prefetched update for this tree and
+// batch (0 when it cannot serve the tree).
+int lines_ncap(const PerTree& t, int64_t n) {
+  const int T = t.num_levels - 1;
+  if (T > kLMaxT) return 0;
+  const int64_t want = n < kLMaxN ? n : kLMaxN;
+  for (int c = (int)((want + 31) / 32 * 32); c >= 32; c -= 32)
+    if (lines_smem(T, c) <= kLinesSmemMax) return c;
+  return 0;
+}
+
+}  // namespace
+
+bool per_update_uses_grid(const PerTree& t, int64_t n) {
+  const int ncap = lines_ncap(t, n);
+  return !(ncap > 0 && n <= (int64_t)kLinesMaxPasses * ncap);
+}
+
 int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, const int64_t* idx,
                             const float* td, int64_t n, const int64_t* count, cudaStream_t stream) {
   UpdateArgs a;
@@ -516,16 +549,8 @@ int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, cons
   // one CTA, passes of `ncap` entries with every line prefetched, while the
   // passes stay few; larger batches take the grid path
   const int T = t.num_levels - 1;
-  int ncap = 0;
-  if (T <= kLMaxT) {
-    const int64_t want = n < kLMaxN ? n : kLMaxN;
-    for (int c = (int)((want + 31) / 32 * 32); c >= 32; c -= 32)
-      if (lines_smem(T, c) <= kLinesSmemMax) {
-        ncap = c;
-        break;
-      }
-  }
-  if (ncap > 0 && n <= (int64_t)kLinesMaxPasses * ncap) {
+  int ncap = lines_ncap(t, n);
+  if (!per_update_uses_grid(t, n)) {
     const void* fl = (const void*)per_update_lines_kernel;
     const size_t smem = lines_smem(T, ncap);
     int rc = per_set_smem(fl, kLinesSmemMax);
