@@ -22,6 +22,15 @@ Metric: sampled transitions per second (sample + gather + IS weights).
             priorities (lognormal(0,2), 1% exact zeros).
   cpu_baseline  the oracle (CPU restatement of the reference's torch
             backend, C, all host threads) on a bounded sample of the same loop.
+  cpu_baseline_sumtree  the reference's own CPU baseline, its float64
+            SumTree (baselines/cpu_sumtree.py) restated in C (one thread, as
+            the reference's per-draw host loop), on this loop and on the
+            100,000-slot CPU configuration, plus the plain-Python restatement
+            (the reference's own code path) on the latter.
+  parity    one 65,536-draw sample of the timed store checked against the
+            oracle: indices equal except excused float32 prefix ties (counted).
+  sharded64m  the sharded configuration (64,000,000 x 74, global batch
+            65,536, strong scaling) on the same N GPUs.
 
 --impl reference times that CPU implementation alone on the same loop.
 
@@ -498,15 +507,86 @@ def time_eager(fn, iters, world):
     return a.elapsed_time(b)
 
 
-def run_sharded(args, world, rank, local):
-    """N>1 (or --workload sharded64m): the sharded buffer across the ranks."""
+def sharded_e2e(sb, gb, rounds, steps, warmup, world, with_add):
+    """The sharded step through the public API, eager, host buffers both
+    ways: H2D of the step's TD errors (and added row), each round sampled into
+    its slot of a device block with sample(..., out=) (in-kernel exchange) and
+    updated, then every slot (rows, idx, w) back to pinned host memory on a
+    copy stream that overlaps the next step (double-buffered blocks)."""
+    dev = sb.device
+    h_td = torch.abs(torch.randn(rounds, gb)).pin_memory()
+    h_row = {k: torch.randn(1, d).pin_memory() for k, d in FIELDS_74.items()}
+    p2p = sb.exchange == "p2p" and gb <= sb.p2p_max_batch
+    sets = []
+    for _ in range(2):
+        d_rows = torch.empty(rounds, gb, ROW_DIM, device=dev)
+        outs = [sb.sample_out(gb, rows=d_rows[r]) for r in range(rounds)] if p2p else None
+        sets.append({"rows": d_rows, "outs": outs, "copied": None,
+                     "h_rows": torch.empty(rounds, gb, ROW_DIM).pin_memory(),
+                     "h_idx": torch.empty(rounds, gb, dtype=torch.int64).pin_memory(),
+                     "h_w": torch.empty(rounds, gb).pin_memory()})
+    st = torch.cuda.current_stream()
+    cs = torch.cuda.Stream(device=dev)
+    k = [0]
+
+    def step():
+        s_ = sets[k[0] % 2]
+        k[0] += 1
+        if s_["copied"] is not None:
+            st.wait_event(s_["copied"])
+        tdd = h_td.to(dev, non_blocking=True)
+        if with_add:
+            sb.add({kk: v.to(dev, non_blocking=True) for kk, v in h_row.items()})
+        results = []
+        for r in range(rounds):
+            res = sb.sample(gb, BETA, out=s_["outs"][r]) if p2p else sb.sample(gb, BETA)
+            sb.update_priorities(res.idx, tdd[r])
+            results.append(res)
+        cs.wait_stream(st)
+        with torch.cuda.stream(cs):
+            for r, res in enumerate(results):
+                if not p2p:
+                    s_["h_rows"][r].copy_(packed_rows(res.views), non_blocking=True)
+                s_["h_idx"][r].copy_(res.idx, non_blocking=True)
+                s_["h_w"][r].copy_(res.w, non_blocking=True)
+            if p2p:
+                s_["h_rows"].copy_(s_["rows"], non_blocking=True)
+            s_["copied"] = torch.cuda.Event()
+            s_["copied"].record(cs)
+
+    for _ in range(warmup):
+        step()
+    n = max(3, min(steps, 20))
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    a.record(st)
+    for _ in range(n):
+        step()
+    st.wait_stream(cs)
+    b.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    e_ms = max_over_ranks(a.elapsed_time(b), world) / n
+    return e_ms, h_td.numel() * 4 + (ROW_DIM * 4 if with_add else 0), rounds * gb * (ROW_DIM * 4 + 12)
+
+
+def sharded_measure(args, world, rank, local, big):
+    """The sharded buffer across the ranks (collective; rank 0 gets the dict).
+
+    big: 64,000,000 x 74 slots split over the ranks (lognormal(0,1)
+    priorities), one step = sample of a global batch of 65,536 -> update of
+    each rank's own draws (strong scaling). Otherwise the weak-scaling UTD
+    loop: 1,000,000 x 74 slots per rank, add 1 per rank + 32 x (sample of
+    256 x N -> update)."""
     dev = torch.device("cuda", local)
-    big = args.workload == "sharded64m"
     total_cap = 64_000_000 if big else CAPACITY * world
     sb = make_sharded(dev, rank, world, total_cap, "lognormal" if big else "absnormal",
                       exchange=args.exchange)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     gb = 65_536 if big else BATCH * world
+    rounds = 1 if big else ROUNDS
     td = torch.randn(ROUNDS, gb, generator=g, device=dev).abs()
     row = {k: torch.randn(1, d, generator=g, device=dev) for k, d in FIELDS_74.items()}
     p2p = sb.exchange == "p2p" and gb <= sb.p2p_max_batch
@@ -516,12 +596,11 @@ def run_sharded(args, world, rank, local):
     per_round = 2 if p2p else 4
     if big:
         fn = lambda: sharded64m_step(sb, td[0], gb)  # noqa: E731
-        per_step = gb
         launches = per_round
     else:
         fn = lambda: sharded_utd_step(sb, row, td, world)  # noqa: E731
-        per_step = BATCH * world * ROUNDS
         launches = 1 + ROUNDS * per_round
+    per_step = gb * rounds
     exchange_desc = ("shard totals and max weight exchanged inside the sample kernel over "
                      "NVLink peer memory (CUDA IPC mailboxes)" if p2p else
                      "NCCL all-gather of shard totals + all-reduce max per sample")
@@ -553,64 +632,63 @@ def run_sharded(args, world, rank, local):
         mode = "eager (host-driven)"
         with ClockSampler(local) as clk:
             ms = time_eager(fn, args.steps, world)
+    graph = None  # release graphs holding NCCL calls before the group is destroyed
     ms = max_over_ranks(ms, world)
     ms_per_step = ms / args.steps
     value = per_step / (ms_per_step / 1e3)
     st = sb.shard.buf.status()
-    bad = st["errors"] or st["timeouts"]
-    bad = max_over_ranks(float(bad), world)
+    bad = max_over_ranks(float(st["errors"] or st["timeouts"]), world)
     if bad:
         raise SystemExit(f"device status reports errors: {st}")
+    e_ms, h2d, d2h = sharded_e2e(sb, gb, rounds, args.steps, 2, world, with_add=not big)
+    sb.close()
+    out = None
     if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong" if big else "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
-            "config": {
-                "workload": ("sharded-64Mx74: sample 65536 beta 0.4 -> update own draws"
-                             if big else
-                             "sharded utd 1Mx74 per rank: add 1 + 32 x (sample 256/rank beta 0.4 "
-                             "-> update own draws)"),
-                "capacity_total": total_cap, "shard_capacity": sb.shard_capacity,
-                "row_dim": ROW_DIM, "global_batch": gb, "rounds": 1 if big else ROUNDS,
-                "parallelism": f"sharded x{world} ({exchange_desc})",
-                "l2": "rows (320 MB per 1M slots) exceed L2",
-                "timing": mode + ", CUDA events, max over ranks"},
+        out = {
+            "value": value, "ms_per_step": ms_per_step,
+            "scaling": "strong" if big else "weak",
+            "workload": ("sharded-64Mx74: sample 65536 beta 0.4 -> update own draws"
+                         if big else
+                         "sharded utd 1Mx74 per rank: add 1 + 32 x (sample 256/rank beta 0.4 "
+                         "-> update own draws)"),
+            "capacity_total": total_cap, "shard_capacity": sb.shard_capacity,
+            "row_dim": ROW_DIM, "global_batch": gb, "rounds": rounds,
+            "parallelism": f"sharded x{world} ({exchange_desc})",
+            "l2": "rows (320 MB per 1M slots) exceed L2",
+            "timing": mode + ", CUDA events, max over ranks",
             "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
+            "e2e": {"value": per_step / (e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         }
-    # e2e: the public API, eager, step inputs from pinned host memory and the
-    # sampled outputs back to pinned host memory
-    h_td = torch.abs(torch.randn(ROUNDS, gb)).pin_memory()
-    h_row = {k: torch.randn(1, d).pin_memory() for k, d in FIELDS_74.items()}
-    rounds = 1 if big else ROUNDS
-    h_out = torch.empty(rounds, gb, ROW_DIM).pin_memory()
-    h_idx = torch.empty(rounds, gb, dtype=torch.int64).pin_memory()
-    h_w = torch.empty(rounds, gb).pin_memory()
+    del sb
+    torch.cuda.empty_cache()
+    return out
 
-    def e2e_step():
-        tdd = h_td.to(dev, non_blocking=True)
-        if not big:
-            sb.add({k: v.to(dev, non_blocking=True) for k, v in h_row.items()})
-        for r in range(rounds):
-            res = sb.sample(gb, BETA)
-            sb.update_priorities(res.idx, tdd[r])
-            h_out[r].copy_(packed_rows(res.views), non_blocking=True)
-            h_idx[r].copy_(res.idx, non_blocking=True)
-            h_w[r].copy_(res.w, non_blocking=True)
 
-    graph = None  # release graphs holding NCCL calls before the group is destroyed
-    for _ in range(3):
-        e2e_step()
-    e_ms = max_over_ranks(time_eager(e2e_step, max(3, min(args.steps, 20)), world), world)
-    e_ms /= max(3, min(args.steps, 20))
+def run_sharded(args, world, rank, local):
+    """N>1 (or --workload sharded64m): the sharded buffer across the ranks.
+    The line carries the weak-scaling UTD loop (N>1) and the 64M strong
+    configuration (`sharded64m`), or the latter alone with --workload."""
+    big_only = args.workload == "sharded64m"
+    main_ = sharded_measure(args, world, rank, local, big=big_only)
+    big = main_ if big_only else sharded_measure(args, world, rank, local, big=True)
     if rank == 0:
-        line["e2e"] = {"value": per_step / (e_ms / 1e3), "unit": UNIT,
-                       "h2d_bytes_per_step": h_td.numel() * 4 + (0 if big else ROW_DIM * 4),
-                       "d2h_bytes_per_step": rounds * gb * (ROW_DIM * 4 + 12)}
+        line = {
+            "metric": METRIC, "value": main_["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": main_["ms_per_step"],
+            "higher_is_better": True, "scaling": main_["scaling"], "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {k: main_[k] for k in ("workload", "capacity_total", "shard_capacity",
+                                             "row_dim", "global_batch", "rounds", "parallelism",
+                                             "l2", "timing")},
+            "gpu_launches": main_["gpu_launches"],
+            "clocks": main_["clocks"],
+            "e2e": main_["e2e"],
+            "sharded64m": {k: big[k] for k in ("value", "ms_per_step", "e2e", "parallelism",
+                                               "timing", "global_batch", "capacity_total")},
+        }
         print(json.dumps(line), flush=True)
-    sb.close()
 
 
 # ---------------------------------------------------------------- CPU side
@@ -664,17 +742,199 @@ def cpu_loop(seconds=None, steps=None, warmup=0, threads=None):
     return ROUNDS * BATCH * n / el, n, threads
 
 
+def sumtree_loop(config: int, seconds: float, impl: str = "c"):
+    """The reference's CPU sum tree (oracle/sumtree.py) on a bounded sample.
+
+    config 0: 100,000 x 74 slots, rounds of sample 256 (beta 0.4) -> gather
+    -> update 256 |N(0,1)| TD errors with ~10% duplicate indices.
+    config 1: 1,000,000 x 74 slots, steps of add 1 + 32 x (sample 256 ->
+    gather -> update 256). impl "c": the C restatement; "python": the plain
+    Python restatement (the reference's own loops). One host thread.
+    Returns (transitions/s, rounds timed)."""
+    from oracle import sumtree
+
+    rng = np.random.default_rng(4 + config)
+    cap = 100_000 if config == 0 else CAPACITY
+    leaves = np.power(np.abs(rng.standard_normal(cap)) + 1e-6, 0.6)
+    if impl == "c":
+        st = sumtree.SumTreeStore(cap, ROW_DIM)
+        st.build_from_leaves(leaves)
+    else:
+        st = sumtree.PySumTree(cap, ROW_DIM)
+        st.tree[cap:] = leaves
+        for k in range(cap - 1, 0, -1):  # set-up, untimed
+            st.tree[k] = st.tree[2 * k] + st.tree[2 * k + 1]
+    st.storage[:] = rng.standard_normal((cap, ROW_DIM), dtype=np.float32)
+    st.size = cap
+    row = rng.standard_normal((1, ROW_DIM), dtype=np.float32)
+    td = np.abs(rng.standard_normal((ROUNDS, BATCH))).astype(np.float32)
+
+    def one_round(r):
+        idx, w = st.sample_from_uniforms(rng.random(BATCH), BETA)[:2]
+        if impl == "c":
+            st.gather(idx)
+        upd = idx.copy()
+        k = BATCH // 10  # ~10% duplicates of other entries of the batch
+        upd[rng.choice(BATCH, k, replace=False)] = upd[rng.integers(0, BATCH, k)]
+        st.update_priorities(upd, td[r % ROUNDS])
+
+    def one_step():
+        if config == 1:
+            if impl == "c":
+                st.add(row)
+            for r in range(ROUNDS):
+                one_round(r)
+        else:
+            one_round(0)
+
+    one_step()  # warm-up
+    rounds_per_step = ROUNDS if config == 1 else 1
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        one_step()
+        n += rounds_per_step
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return BATCH * n / el, n
+
+
+def cpu_sumtree_baseline(seconds: float):
+    """cpu_baseline_sumtree of the bench line (see the module docstring)."""
+    v1, n1 = sumtree_loop(1, seconds, "c")
+    v0, n0 = sumtree_loop(0, seconds / 2, "c")
+    p0, m0 = sumtree_loop(0, seconds / 2, "python")
+    return {
+        "value": v1, "unit": UNIT, "cores": 1, "host_cores": os.cpu_count(), "threads": 1,
+        "kind": "port",
+        "impl": "the reference's float64 SumTree (baselines/cpu_sumtree.py) restated in C, "
+                "one draw and one index at a time on one host thread",
+        "sample": f"{n1} sample 256 + update 256 rounds of this loop (1M x 74, add 1 per 32 rounds)",
+        "config0_100Kx74": {"value": v0, "rounds": n0,
+                            "python_loop_value": p0, "python_loop_rounds": m0,
+                            "workload": "sample 256 beta 0.4 -> update 256, ~10% duplicate indices"},
+    }
+
+
+def parity_check(buf, batch=65536, seed=21):
+    """One `batch`-draw sample of the store checked against the oracle: the
+    excused float32 prefix ties are counted; any other index mismatch fails
+    the run. Test-side checker (the oracle is not timed)."""
+    from oracle import oracle
+
+    g = torch.Generator(device=buf.device).manual_seed(seed)
+    rand = torch.rand(batch, generator=g, device=buf.device)
+    _, idx, _ = buf.sample_from_uniforms(rand, BETA)
+    torch.cuda.synchronize()
+    size = int(buf._size_cursor[0].item())
+    lv = buf.priorities.cpu().numpy()
+    rnp = rand.cpu().numpy()
+    idx_o, _, csum = oracle.sample(lv, buf.capacity, size, rnp, BETA, nthreads=os.cpu_count() or 1)
+    eq, excused, bad = oracle.classify_indices(idx.cpu().numpy(), idx_o, rnp, csum, size)
+    if bad.size:
+        raise SystemExit(f"parity: {bad.size} index mismatches outside float32 ties")
+    return {"draws": batch, "equal": eq, "excused_ties": excused, "mismatches": 0,
+            "store": "the timed 1M x 74 store after the loop", "checker": "oracle (C)"}
+
+
+class HostPriorityBuffer:
+    """PERBuffer API over priorities kept and searched on the host: the
+    reference's CPU baselines restated under oracle/ (checker code, used
+    here only as the comparison arms of the replay-share profile). Rows live
+    on the GPU and are gathered there, as in the reference's CpuSumTreePER
+    (cpu_sumtree.py:41-97): each sample walks the host structure and sends the
+    indices and weights over PCIe; each update brings the TD errors back.
+
+    kind "cpu_sumtree": the float64 SumTree (C restatement, one draw at a
+    time); kind "torch_cpu": the reference torch backend's algorithm (C
+    restatement: full cumsum of the priorities per sample, all host threads)."""
+
+    def __init__(self, capacity, fields, device, kind):
+        from oracle import oracle, sumtree
+
+        self.kind = kind
+        self.capacity = capacity
+        self.device = torch.device(device)
+        self.fields = dict(fields)
+        self._offsets, o = {}, 0
+        for name, d in fields.items():
+            self._offsets[name] = (o, o + d)
+            o += d
+        self.storage = torch.zeros(capacity, o, device=self.device)
+        self.cursor = 0
+        self.size = 0
+        self._rng = np.random.default_rng(0)
+        self._oracle = oracle
+        self._threads = os.cpu_count() or 1
+        if kind == "cpu_sumtree":
+            self.st = sumtree.SumTreeStore(capacity, 1)
+        else:
+            self.st = oracle.OracleStore(capacity, {"x": 1})
+
+    def add(self, batch):
+        n = next(iter(batch.values())).shape[0]
+        idx = (torch.arange(n, device=self.device) + self.cursor) % self.capacity
+        for name, (a, b) in self._offsets.items():
+            self.storage[idx, a:b] = batch[name].reshape(n, -1).to(self.storage.dtype)
+        if self.kind == "cpu_sumtree":
+            self.st.add(np.zeros((n, 1), np.float32))
+        else:
+            self.st.add({"x": np.zeros((n, 1), np.float32)})
+        self.cursor = (self.cursor + n) % self.capacity
+        self.size = min(self.size + n, self.capacity)
+
+    def sample(self, batch_size, beta=0.4):
+        if self.kind == "cpu_sumtree":
+            idx, w = self.st.sample_from_uniforms(self._rng.random(batch_size), beta)
+        else:
+            idx, w, _ = self._oracle.sample(self.st.priorities, self.capacity, self.size,
+                                            self._rng.random(batch_size, dtype=np.float32), beta,
+                                            nthreads=self._threads)
+        idx_t = torch.from_numpy(idx).to(self.device)
+        out = self.storage[idx_t]
+        views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
+        return views, idx_t, torch.from_numpy(w).to(self.device)
+
+    def update_priorities(self, indices, td_errors):
+        self.st.update_priorities(indices.cpu().numpy(),
+                                  td_errors.detach().reshape(-1).abs().cpu().numpy())
+
+
+def replay_share_arms(steps=20):
+    """The UTD replay-share profile (per_b200.profile_utd: SAC-style learner,
+    2 critics, UTD 32, batch 256, 1M slots) with this engine and with the
+    reference's two CPU baselines as the replay backend, every arm timed the
+    reference's way (host clock around synchronised phases); the engine also
+    by CUDA events (device timeline, nothing synchronised)."""
+    from per_b200 import profile_utd
+
+    fields = {"obs": 32, "action": 8, "reward": 1, "next_obs": 32, "done": 1}
+    keep = ("replay_share", "replay_us_per_grad_step", "learn_ms", "replay_ms", "step_ms", "timing")
+    out = {}
+    r = profile_utd.run(steps=steps, warmup=3, timing="events")
+    out["b200_events"] = {k: r[k] for k in keep}
+    r = profile_utd.run(steps=steps, warmup=3, timing="wall")
+    out["b200_wall"] = {k: r[k] for k in keep}
+    for kind, n in (("cpu_sumtree", max(2, steps // 4)), ("torch_cpu", max(2, steps // 4))):
+        buf = HostPriorityBuffer(1_000_000, fields, "cuda", kind)
+        r = profile_utd.run(steps=n, warmup=1, timing="wall", buffer=buf)
+        out[kind] = {k: r[k] for k in keep}
+        del buf
+    out["config"] = "utd 32, batch 256, 1M slots (200k filled), 2 critics, SAC-style update"
+    return out
+
+
 # ---------------------------------------------------------------- main
-def traffic_from_profiles(key="traffic_bytes_per_launch_b256", name="sample_kernel_1Mx74.md"):
-    """dram bytes per launch from a committed ncu summary (one ncu capture)."""
-    p = os.path.join(ROOT, "profiles", name)
+def traffic_from_profiles(key: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum of
+    one ncu capture) from profiles/traffic.json, or None."""
     try:
-        for line in open(p):
-            if line.startswith(key + ":"):
-                return int(float(line.split(":", 1)[1]))
-    except OSError:
-        pass
-    return None
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            v = json.load(f).get(key)
+        return int(v) if v is not None else None
+    except (OSError, ValueError):
+        return None
 
 
 def run_reference(args, world, rank):
@@ -693,6 +953,8 @@ def run_reference(args, world, rank):
                          "sample": f"{n} full steps ({n * ROUNDS} sample+update rounds) of the loop, "
                                    "oracle restatement of the reference torch backend in C"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        # the reference's other CPU baseline (its float64 SumTree), same loop
+        "cpu_baseline_sumtree": cpu_sumtree_baseline(4.0),
     }
     print(json.dumps(line), flush=True)
 
@@ -707,6 +969,10 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-share", action="store_true",
+                    help="skip the replay-share profile of the N=1 line")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the sharded 64M x 74 configuration of the N=1 line")
     ap.add_argument("--workload", default="utd", choices=["utd", "sharded64m"])
     ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "nccl"],
                     help="sharded mode: in-kernel peer-memory exchange or NCCL collectives")
@@ -775,7 +1041,7 @@ def main():
     ab = algo_bytes(BATCH, ROW_DIM)
     achieved = ab / (k_us * 1e-6) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": traffic_from_profiles(),
+                "frac": achieved / peak, "traffic": traffic_from_profiles("sample_1Mx74_b256"),
                 "peak_source": peak_kind, "kernel": "per_sample_kernel_r112 (fused sample, 112-register build)",
                 "kernel_us": k_us, "algo_bytes_per_launch": ab, "batch": BATCH}
     # the same kernel at the large-batch end of the sweep (1M x 74, batch 65,536)
@@ -784,7 +1050,7 @@ def main():
     a64 = ab64 / (k64 * 1e-6) / 1e9
     roofline_large = {"bound": "hbm", "achieved": a64, "peak": peak, "unit": "GB/s",
                       "frac": a64 / peak, "peak_source": peak_kind, "kernel": "per_sample_kernel_r112 (fused sample, 112-register build)",
-                      "traffic": traffic_from_profiles("traffic_bytes_per_launch_b65536"),
+                      "traffic": traffic_from_profiles("sample_1Mx74_b65536"),
                       "kernel_us": k64, "algo_bytes_per_launch": ab64, "batch": 65536}
 
     sweep = None
@@ -828,12 +1094,28 @@ def main():
         e2e = {"value": ROUNDS * BATCH * world / (e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
-    cpu = None
+    # the CPU legs (host cores; the oracle and the reference's sum tree are
+    # timed here, and the oracle checks one large sample of the timed store)
+    cpu = cpu_st = parity = share = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, n, threads = cpu_loop(seconds=args.cpu_seconds, warmup=1)
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{n} steps ({n * ROUNDS} sample 256 + update 256 rounds) of the same "
                          "loop, oracle (reference torch-backend algorithm) in C"}
+        cpu_st = cpu_sumtree_baseline(args.cpu_seconds / 2)
+        parity = parity_check(buf)
+        if not args.no_share:
+            share = replay_share_arms()
+
+    sh64 = None
+    if not args.no_sharded:
+        del buf
+        graph = None
+        torch.cuda.empty_cache()
+        big = sharded_measure(args, world, rank, local, big=True)
+        if rank == 0:
+            sh64 = {k: big[k] for k in ("value", "ms_per_step", "e2e", "parallelism", "timing",
+                                        "global_batch", "capacity_total")}
 
     if rank == 0:
         line = {
@@ -850,6 +1132,10 @@ def main():
             "sweep": sweep,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "cpu_baseline_sumtree": cpu_st,
+            "parity": parity,
+            "utd_replay_share": share,
+            "sharded64m": sh64,
             "gpu_launches": (1 + 2 * ROUNDS) * args.steps,
             "clocks": clk.summary(),
         }

@@ -12,8 +12,9 @@ import pytest
 import torch
 
 import cases
-from helpers import SUM_RTOL, check_sample, check_tree, make_buffer, packed_rows
+from helpers import SUM_RTOL, W_RTOL, check_sample, check_tree, make_buffer, packed_rows
 from oracle import oracle
+from per_b200 import PERBuffer
 
 pytestmark = pytest.mark.gpu
 
@@ -107,6 +108,13 @@ def _leaves(rng, n, kind):
     return rng.lognormal(0.0, 1.0, n).astype(np.float32)
 
 
+def tie_bound(b: int) -> int:
+    """Most excused float32 prefix ties a batch of b draws may show: about 1.5x
+    the rate measured on these stores (~2%, e.g. 1,280 of 65,536 heavy-tailed
+    draws) plus four binomial standard deviations."""
+    return int(0.03 * b + 4.0 * (0.02 * b) ** 0.5 + 3)
+
+
 @pytest.mark.parametrize("kind,batches", [
     ("absnormal", [256, 4096]),
     ("heavy", [32, 128, 512, 2048, 8192, 32768, 65536]),
@@ -123,7 +131,7 @@ def test_full_size_1m_x_74(kind, batches):
         rand = rng.random(b, dtype=np.float32)
         r = check_sample(buf, rows, leaves, cap, rand, 0.4, tag=f"{kind} B={b}")
         print(f"PARITY 1Mx74 {kind} B={b}: {r}")
-        assert r["excused"] <= max(3, b // 20)
+        assert r["excused"] <= tie_bound(b)
     st = buf.status()
     assert st["errors"] == 0 and st["timeouts"] == 0
 
@@ -159,6 +167,40 @@ def test_wide_rows_gather_bit_exact():
     buf = make_buffer(cap, {"img": 4096}, {"img": rows}, leaves)
     r = check_sample(buf, rows, leaves, cap, rng.random(1024, dtype=np.float32), 0.6)
     assert r["equal"] + r["excused"] == 1024
+
+
+def test_wide_rows_full_config_2m_x_4096():
+    """The wide-row configuration at its full size: 2,000,000 x 4096 float32
+    rows (32.8 GB, more than 2^31 row elements, 16 KB rows copied inside the
+    sample kernel), batch 1024, beta 0.6. Rows are checked on the device
+    against the stored rows they name; indices and weights against the
+    oracle on the same leaves and uniforms."""
+    cap, dim, b = 2_000_000, 4096, 1024
+    dev = torch.device("cuda")
+    buf = PERBuffer(cap, {"feat": dim}, device=dev)
+    g = torch.Generator(device=dev).manual_seed(31)
+    for s0 in range(0, cap, 100_000):
+        buf.add({"feat": torch.rand(100_000, dim, generator=g, device=dev)})
+    leaves = ((torch.randn(cap, generator=g, device=dev).abs() + 1e-6) ** 0.6)
+    buf.priorities[:cap] = leaves
+    buf.rebuild_sums()
+    rand = torch.rand(b, generator=g, device=dev)
+    views, idx, w = buf.sample_from_uniforms(rand, 0.6)
+    torch.cuda.synchronize()
+    assert torch.equal(views["feat"], buf.storage[idx])  # rows bit-exact (device-side check)
+    assert int(idx.max()) * dim >= 2**31  # offsets past 2^31 elements are exercised
+    lv = np.zeros(buf.capacity_padded, np.float32)
+    lv[:cap] = leaves.cpu().numpy()
+    rnp = rand.cpu().numpy()
+    idx_o, _, csum = oracle.sample(lv, cap, cap, rnp, 0.6)
+    eq, exc, bad = oracle.classify_indices(idx.cpu().numpy(), idx_o, rnp, csum, cap)
+    assert bad.size == 0 and exc <= tie_bound(b)
+    w_ref = oracle.weights_for(lv, csum[-1], cap, idx.cpu().numpy(), 0.6)
+    np.testing.assert_allclose(w.cpu().numpy(), w_ref, rtol=W_RTOL, atol=0)
+    st = buf.status()
+    assert st["errors"] == 0 and st["timeouts"] == 0
+    del views, buf
+    torch.cuda.empty_cache()
 
 
 @pytest.mark.parametrize("row_dim", [1, 2, 3, 4, 5, 8, 64, 74, 127, 128, 129, 300, 522,

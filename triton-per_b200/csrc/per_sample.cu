@@ -216,57 +216,6 @@ __device__ __forceinline__ int search32(const float* c, double r, double* ex, fl
   return 4 * kq + j;
 }
 
-// The leaf level: only the child and its value are needed (no residual for
-// a level below). A float32 prefix of the 32 children decides whenever r lies
-// farther than a rounding margin from both ends of the chosen child's range;
-// otherwise (r within the margin of a boundary, at or past the node's sum, an
-// empty node) the exact float64 search32 decides. The float32 partial sums
-// take at most 12 additions of non-negative values, so each is within
-// 12 u S of its exact value (u = 2^-24, S = the children's sum), and
-// (float)r within u S of r; the margin is 64 u S, so the fast answer is the
-// exact one whenever it is taken.
-__device__ __forceinline__ int search32_leaf(const float* c, double r, float* val, bool* fb) {
-  float P[9];
-  P[0] = 0.f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) P[k + 1] = P[k] + ((c[4 * k] + c[4 * k + 1]) + (c[4 * k + 2] + c[4 * k + 3]));
-  const float rf = __double2float_rn(r);
-  const float M = P[8] * 3.814697265625e-06f;  // 64 * 2^-24
-  int kq = 8;
-#pragma unroll
-  for (int k = 7; k >= 0; --k)
-    if (P[k + 1] > rf) kq = k;
-  float base = 0.f, top = P[8], e0 = c[0], e1 = c[1], e2 = c[2];
-#pragma unroll
-  for (int k = 1; k < 8; ++k)
-    if (k == kq) {
-      base = P[k];
-      e0 = c[4 * k];
-      e1 = c[4 * k + 1];
-      e2 = c[4 * k + 2];
-    }
-#pragma unroll
-  for (int k = 0; k < 8; ++k)
-    if (k == kq) top = P[k + 1];
-  const float s1 = base + e0, s2 = s1 + e1, s3 = s2 + e2;
-  const int j = s1 > rf ? 0 : s2 > rf ? 1 : s3 > rf ? 2 : 3;
-  const float lo = j == 0 ? base : j == 1 ? s1 : j == 2 ? s2 : s3;
-  const float hi = j == 0 ? s1 : j == 1 ? s2 : j == 2 ? s3 : top;
-  // the lower end of child 0 of quad 0 is exactly 0 <= r
-  const bool ok = kq < 8 && hi - rf > M && (kq == 0 && j == 0 ? true : rf - lo > M);
-  if (!ok) {
-    double ex;
-    return search32(c, r, &ex, val, fb);
-  }
-  const int f = 4 * kq + j;
-  float v = c[0];
-#pragma unroll
-  for (int i = 1; i < 32; ++i)
-    if (i == f) v = c[i];
-  *val = v;
-  return f;
-}
-
 template <int VEC>
 struct VecT;
 template <>
@@ -513,8 +462,9 @@ __device__ __forceinline__ void wide_copy(const SampleArgs& a, unsigned char* st
 }
 
 // The sample kernel's body; two kernels below run it with different register
-// budgets.
-template <int VEC, bool SHARDED>
+// budgets. WIDE: rows wider than a warp's staging tile, copied by bulk copies
+// (a build of its own, so that the other builds carry none of that code).
+template <int VEC, bool SHARDED, bool WIDE = false>
 __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorMap& rows_map) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double s_wsum[kMaxWarps + 1];
@@ -539,7 +489,7 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   const int nthreads = blockDim.x;
   const int nwarps = (nthreads >> 5) - 1;  // compute warps; the last warp is the helper
   const bool helper = warp == nwarps;
-  const int D = a.draws_per_warp;  // draws per warp and tile: 32, fewer for wide rows
+  const int D = WIDE ? a.draws_per_warp : 32;  // draws per warp and tile (fewer for wide rows)
   const int64_t tile_draws = (int64_t)nwarps * D;
   const PerTree& t = a.t;
   PerScratch* sc = t.scratch;
@@ -551,7 +501,7 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   // stage_bytes are multiples of 128); otherwise one bulk copy per row
   const bool g4 = a.gather4 && (per_smem_addr(smem) & 127u) == 0u;
   uint32_t phase = 0u;
-  if (!helper && (a.use_bulk || a.wide) && lane == 0) {
+  if (!helper && (a.use_bulk || WIDE) && lane == 0) {
     per_mbar_init(&s_mbar[warp], 1);
     per_fence_mbar_init();
   }
@@ -730,9 +680,43 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
       if (SHARDED) per_st_relaxed_u64(&slots[2 * blockIdx.x + 1], ((unsigned long long)tag << 32) | s_cta_own);
     }
     if (gridDim.x <= kAllToAllCtas || blockIdx.x == 0) {
-      // small grids: every helper reads all slots; large grids: CTA 0 does
-      // and publishes two tagged totals
-      timed_out = !gather_slots<SHARDED>(slots, (int)gridDim.x, tag, lane, &mb, &owned);
+      // small grids: every helper reads all slots (at most two per lane, a
+      // short poll loop); large grids: CTA 0 does, every lane issuing all its
+      // loads of a poll together (gather_slots), and publishes two tagged totals
+      if (gridDim.x > kAllToAllCtas) {
+        timed_out = !gather_slots<SHARDED>(slots, (int)gridDim.x, tag, lane, &mb, &owned);
+      } else {
+        constexpr int kPer = kMaxGrid / 32;
+        static_assert(kPer <= 64, "one pending bit per slot of a lane");
+        unsigned long long pending = 0ull;  // bit i: slot lane + 32 i not seen yet
+        for (int i = 0; i < kPer && lane + 32 * i < (int)gridDim.x; ++i) pending |= 1ull << i;
+        for (uint32_t it = 0; __any_sync(PER_FULL_MASK, pending != 0ull); ++it) {
+          if (it > PER_SPIN_LIMIT) {
+            timed_out = true;
+            break;
+          }
+          unsigned long long left = pending;
+          while (left) {
+            const int i = __ffsll((long long)left) - 1;
+            left &= left - 1;
+            const int c = lane + 32 * i;
+            const unsigned long long v = per_ld_relaxed_u64(&slots[2 * c]);
+            const unsigned long long n = SHARDED ? per_ld_relaxed_u64(&slots[2 * c + 1])
+                                                 : ((unsigned long long)tag << 32);
+            if ((uint32_t)(v >> 32) == tag && (uint32_t)(n >> 32) == tag) {
+              mb = max(mb, (uint32_t)v);
+              owned += (uint32_t)n;
+              pending &= ~(1ull << i);
+            }
+          }
+          if (pending) __nanosleep(PER_SPIN_SLEEP_NS);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          mb = max(mb, __shfl_xor_sync(PER_FULL_MASK, mb, o));
+          owned += __shfl_xor_sync(PER_FULL_MASK, owned, o);
+        }
+      }
       if (lane == 0 && blockIdx.x == 0) {  // all CTAs have read gen: next generation
         if (SHARDED) sc->draws[(gen + 1u) & 1u] = 0ull;
         sc->mx_gen = gen + 1u;
@@ -939,10 +923,10 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     r -= s_pre[ppos(k)];
     float p = 0.f;
 
-    // lower levels: stage each draw's 32 children, search them per lane (the
-    // leaf level through the float32 fast path). Only lanes with a draw (lanes
-    // 0 .. nact-1) fetch lines: idle lanes would all walk toward slot 0 and
-    // pile onto one L2 line; their search reads stale lines and is discarded.
+    // lower levels: stage each draw's 32 children, search them per lane. Only
+    // lanes with a draw (lanes 0 .. nact-1) fetch lines: idle lanes would all
+    // walk toward slot 0 and pile onto one L2 line; their search reads stale
+    // lines and is discarded.
     const int nact = __popc(__ballot_sync(PER_FULL_MASK, ok));
     for (int L = top - 1; L >= 0; --L) {
       __syncwarp();
@@ -958,14 +942,9 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
         c[4 * i + 2] = v.z;
         c[4 * i + 3] = v.w;
       }
-      int f;
-      if (L == 0) {
-        f = search32_leaf(c, r, &p, &fb);
-      } else {
-        double ex;
-        f = search32(c, r, &ex, &p, &fb);
-        r -= ex;
-      }
+      double ex;
+      const int f = search32(c, r, &ex, &p, &fb);
+      r -= ex;
       node = node * PER_FANOUT + f;
     }
 
@@ -1061,8 +1040,8 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
         if (r0 > 0) gather_issue(a, stage, s_rows[warp], r0, rn, lane, &s_mbar[warp], g4, &rows_map);
         gather_finish<VEC>(a, stage, row0 + r0, rn, lane, &s_mbar[warp], phase);
       }
-    } else if (!SHARDED && a.wide && nrows > 0) {
-      wide_copy(a, stage, i, j, lane, nrows, &s_mbar[warp], phase);
+    } else if constexpr (WIDE) {
+      if (nrows > 0) wide_copy(a, stage, i, j, lane, nrows, &s_mbar[warp], phase);
     }  // other rows wider than a stage: per_gather_rows_kernel after this kernel
   }
 
@@ -1097,7 +1076,7 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     const bool last = tl + gridDim.x >= a.num_tiles;
     if (lane < D && j < a.batch) a.w[j] = __fdiv_rn(last ? w_last : a.w[j], gmax);
   }
-  if (a.wide) bulk_wait_all();  // the last row stores are complete before the CTA exits
+  if constexpr (WIDE) bulk_wait_all();  // the last row stores are complete before the CTA exits
 }
 
 // CTAs of up to kMaxWarps + 1 warps, two per SM: the register allocator
@@ -1106,6 +1085,13 @@ template <int VEC, bool SHARDED>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 2)
     per_sample_kernel(SampleArgs a, const __grid_constant__ CUtensorMap rows_map) {
   sample_body<VEC, SHARDED>(a, rows_map);
+}
+
+// Rows wider than a warp's staging tile (wide mode), 112 registers.
+template <int VEC>
+__global__ void __maxnreg__(112)
+    per_sample_kernel_wide(SampleArgs a, const __grid_constant__ CUtensorMap rows_map) {
+  sample_body<VEC, false, true>(a, rows_map);
 }
 
 // CTAs of up to kR112Warps warps (helper included), two per SM at 112
@@ -1270,7 +1256,7 @@ constexpr size_t kWideSmem = 200 * 1024;
 
 template <int VEC>
 int launch_wide(SampleArgs a, cudaStream_t stream) {
-  const void* fn = (const void*)per_sample_kernel_r112<VEC, false>;
+  const void* fn = (const void*)per_sample_kernel_wide<VEC>;
   int dev = 0, sms = 148;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -87,6 +87,21 @@ class Engine {
     return py::make_tuple(rc, views(out), idx, w, pos, count);
   }
 
+  // sample_sharded_p2p into caller-owned device buffers -> rc (rows
+  // row_stride elements apart, idx int64, w float32, pos int32, count int64[1])
+  int sample_sharded_p2p_into(int32_t rank, int32_t world, int64_t shard_base, int64_t mailboxes,
+                              int64_t batch, double beta, uint64_t seed, int64_t counter,
+                              int64_t rows_ptr, int64_t row_stride, int64_t idx, int64_t w,
+                              int64_t pos, int64_t count) {
+    c10::cuda::CUDAGuard guard(device_);
+    return per_sample_sharded_p2p_rng(
+        store_, rank, world, shard_base, reinterpret_cast<void* const*>(mailboxes), seed,
+        reinterpret_cast<uint64_t*>(counter), batch, static_cast<float>(beta),
+        reinterpret_cast<float*>(rows_ptr), row_stride, reinterpret_cast<int64_t*>(idx),
+        reinterpret_cast<float*>(w), reinterpret_cast<int32_t*>(pos),
+        reinterpret_cast<int64_t*>(count), stream());
+  }
+
   // sharded update of the first *count entries (global indices) -> rc
   int update_shard_count(int64_t base, const at::Tensor& idx, const at::Tensor& td,
                          const at::Tensor& count) {
@@ -145,5 +160,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("sample_from", &Engine::sample_from)
       .def("update", &Engine::update)
       .def("sample_sharded_p2p", &Engine::sample_sharded_p2p)
+      .def("sample_sharded_p2p_into", &Engine::sample_sharded_p2p_into)
       .def("update_shard_count", &Engine::update_shard_count);
 }

@@ -15,12 +15,19 @@ CUDA events on the stream and nothing synchronises inside the loop, so the
 share is the replay's part of the device timeline as the learner actually
 runs it (the host enqueues ahead). `--trace` exports a torch.profiler Chrome
 trace of a few steps.
+
+run(buffer=..., timing="wall") drives any buffer with the PERBuffer API (for
+instance a host-side baseline whose priorities live on the CPU) and times
+each phase with the host clock around synchronised calls, the method of the
+reference's profiler (bench/profile_utd.py:76-97), so that engines whose work
+is partly on the host compare on equal terms.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import time
 
 import torch
 import torch.nn as nn
@@ -54,11 +61,18 @@ class Learner:
 
 def run(utd: int = 32, batch_size: int = 256, capacity: int = 1_000_000, obs_dim: int = 32,
         act_dim: int = 8, num_q: int = 2, steps: int = 60, warmup: int = 10, fill: int = 200_000,
-        device: str = "cuda", trace: str | None = None, seed: int = 0) -> dict:
+        device: str = "cuda", trace: str | None = None, seed: int = 0, buffer=None,
+        timing: str = "events") -> dict:
+    """buffer: a buffer with the PERBuffer API built for these fields and
+    capacity (default: this engine's PERBuffer). timing "events": CUDA events
+    on the stream, nothing synchronised; "wall": host clock around
+    synchronised phases."""
+    if timing not in ("events", "wall"):
+        raise ValueError(f"timing must be 'events' or 'wall', not {timing!r}")
     torch.manual_seed(seed)
     dev = torch.device(device)
     fields = {"obs": obs_dim, "action": act_dim, "reward": 1, "next_obs": obs_dim, "done": 1}
-    buf = PERBuffer(capacity, fields, device=dev)
+    buf = buffer if buffer is not None else PERBuffer(capacity, fields, device=dev)
     n = min(capacity, fill)
     buf.add({k: torch.randn(n, d, device=dev) for k, d in fields.items()})
     learner = Learner(obs_dim, act_dim, num_q, dev)
@@ -66,10 +80,28 @@ def run(utd: int = 32, batch_size: int = 256, capacity: int = 1_000_000, obs_dim
 
     stream = torch.cuda.current_stream(dev)
     marks = []  # per gradient step: (start, sampled, learned, updated) events
+    wall = {"replay": 0.0, "learn": 0.0, "n": 0}  # timing "wall": seconds
 
     def env_step(record: bool):
         buf.add(new_row)
         for _ in range(utd):
+            if timing == "wall":
+                torch.cuda.synchronize(dev)
+                t0 = time.perf_counter()
+                batch, idx, w = buf.sample(batch_size)
+                torch.cuda.synchronize(dev)
+                t1 = time.perf_counter()
+                td = learner.step(batch, w)
+                torch.cuda.synchronize(dev)
+                t2 = time.perf_counter()
+                buf.update_priorities(idx, td)
+                torch.cuda.synchronize(dev)
+                t3 = time.perf_counter()
+                if record:
+                    wall["replay"] += (t1 - t0) + (t3 - t2)
+                    wall["learn"] += t2 - t1
+                    wall["n"] += 1
+                continue
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if record else None
             if record:
                 ev[0].record(stream)
@@ -99,14 +131,19 @@ def run(utd: int = 32, batch_size: int = 256, capacity: int = 1_000_000, obs_dim
     for e0, e1, e2, e3 in marks:
         replay += e0.elapsed_time(e1) + e2.elapsed_time(e3)
         learn += e1.elapsed_time(e2)
-    wall = total.elapsed_time(end)
+    n_grad = len(marks)
+    if timing == "wall":
+        replay, learn, n_grad = 1e3 * wall["replay"], 1e3 * wall["learn"], wall["n"]
+    elapsed = total.elapsed_time(end)
     result = {
         "utd": utd, "batch_size": batch_size, "capacity": capacity, "num_q": num_q,
-        "steps": steps, "replay_ms": replay, "learn_ms": learn, "step_ms": wall / steps,
+        "steps": steps, "timing": timing, "replay_ms": replay, "learn_ms": learn,
+        "step_ms": elapsed / steps,
         "replay_share": replay / (replay + learn) if replay + learn > 0 else 0.0,
-        "replay_us_per_grad_step": 1e3 * replay / max(1, len(marks)),
-        "status": buf.status(),
+        "replay_us_per_grad_step": 1e3 * replay / max(1, n_grad),
     }
+    if hasattr(buf, "status"):
+        result["status"] = buf.status()
 
     if trace:
         from torch.profiler import ProfilerActivity, profile
@@ -132,10 +169,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--trace", default=None, help="Chrome trace output path")
+    ap.add_argument("--timing", default="events", choices=["events", "wall"])
     args = ap.parse_args()
     print(json.dumps(run(args.utd, args.batch_size, args.capacity, args.obs_dim, args.act_dim,
                          args.num_q, args.steps, args.warmup, device=args.device,
-                         trace=args.trace)))
+                         trace=args.trace, timing=args.timing)))
 
 
 if __name__ == "__main__":

@@ -59,6 +59,33 @@ class ShardSample(NamedTuple):
     pos: torch.Tensor    # int32[batch_size] positions of those draws in the global batch
 
 
+class ShardSampleOut:
+    """Caller-owned destination of one sharded sample (device tensors of the
+    global batch size): rows with per-field views, idx (with the owned count
+    stored right behind it), w and pos. Made by ShardedPERBuffer.sample_out();
+    sample(..., out=) then allocates nothing."""
+
+    def __init__(self, owner: "ShardedPERBuffer", batch: int, rows=None):
+        if batch < 1:
+            raise ValueError("batch must be positive")
+        dev = owner.device
+        if rows is None:
+            rows = torch.empty(batch, owner.row_dim, device=dev)
+        if rows.device != dev or rows.dtype != torch.float32 or \
+                tuple(rows.shape) != (batch, owner.row_dim) or rows.stride(1) != 1:
+            raise ValueError(f"rows must be [{batch}, {owner.row_dim}] float32 on {dev} "
+                             "with unit column stride")
+        self.owner = owner
+        self.batch = batch
+        self.rows = rows
+        self._idx_count = torch.empty(batch + 1, dtype=torch.int64, device=dev)
+        self.idx = self._idx_count[:batch]
+        self.count = self._idx_count[batch:]
+        self.w = torch.empty(batch, device=dev)
+        self.pos = torch.empty(batch, dtype=torch.int32, device=dev)
+        self.views = owner._views(rows)
+
+
 class CudaShard:
     """The rank's shard on its GPU: a PERBuffer driven through the C ABI."""
 
@@ -98,6 +125,21 @@ class CudaShard:
                     idx.data_ptr(), w.data_ptr(), pos.data_ptr(), count.data_ptr(),
                     lmax.data_ptr(), _stream_ptr(dev)))
         return out, idx, w, pos, count, lmax
+
+    def sample_p2p_into(self, rank, world, base, mailboxes, beta, rng, out: ShardSampleOut):
+        """sample_p2p with in-kernel uniforms into a caller-owned destination."""
+        buf = self.buf
+        args = (rank, world, base, mailboxes.data_ptr(), out.batch, float(beta), rng[0],
+                rng[1].data_ptr(), out.rows.data_ptr(), out.rows.stride(0), out.idx.data_ptr(),
+                out.w.data_ptr(), out.pos.data_ptr(), out.count.data_ptr())
+        if buf._engine is not None:
+            rc = buf._engine.sample_sharded_p2p_into(*args)
+            if rc:
+                _lib.check("per_sample_sharded_p2p_rng", rc)
+        else:
+            buf._call("per_sample_sharded_p2p_rng", _lib.lib.per_sample_sharded_p2p_rng,
+                      buf._store_ref, args[0], args[1], args[2], args[3], args[6], args[7],
+                      args[4], args[5], args[8], args[9], args[10], args[11], args[12], args[13])
 
     def sample_p2p(self, rank, world, base, mailboxes, rand, beta, rng=None, batch=None):
         b = rand.numel() if rng is None else batch
@@ -309,8 +351,29 @@ class ShardedPERBuffer:
         self.shard.add(batch)
 
     # --------------------------------------------------------------- sample
-    def sample(self, batch_size: int, beta: float = 0.4) -> ShardSample:
-        """Collective: this rank's share of a global batch of `batch_size` draws."""
+    def sample_out(self, batch_size: int, rows: torch.Tensor | None = None) -> ShardSampleOut:
+        """A reusable destination for sample(batch_size, beta, out=...); `rows`
+        may be a view into the caller's own buffer (e.g. one slot of a
+        [rounds, batch, row_dim] block that goes to the host in one copy)."""
+        return ShardSampleOut(self, int(batch_size), rows)
+
+    def sample(self, batch_size: int, beta: float = 0.4,
+               out: ShardSampleOut | None = None) -> ShardSample:
+        """Collective: this rank's share of a global batch of `batch_size` draws.
+
+        With `out` (from sample_out(); in-kernel exchange only, batch up to
+        p2p_max_batch) the draws are written into that destination and nothing
+        is allocated."""
+        if out is not None:
+            if out.owner is not self or out.batch != int(batch_size):
+                raise ValueError("out was made by sample_out() of another buffer or batch size")
+            if self.exchange != "p2p" or out.batch > self.p2p_max_batch:
+                raise ValueError("sample(out=) needs the in-kernel exchange and a batch of at "
+                                 f"most p2p_max_batch ({self.p2p_max_batch})")
+            self.shard.sample_p2p_into(self.rank, self.world, self.base, self._mailboxes, beta,
+                                       (self.seed, self._rng_counter), out)
+            self._last = (out.idx, out.count)
+            return ShardSample(out.views, out.idx, out.w, out.count, out.pos)
         if not isinstance(self.shard, CudaShard):
             rand = torch.rand(batch_size, generator=self._gen, device=self.device)
             return self.sample_from_uniforms(rand, beta)
