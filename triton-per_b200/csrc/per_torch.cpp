@@ -111,6 +111,22 @@ class Engine {
                                              count.data_ptr<int64_t>(), stream());
   }
 
+  // update_priorities(indices, td_errors) as the caller passes them: when both
+  // are already what the C ABI takes (int64 / float32, contiguous, on this
+  // device, as many TD errors as indices) -> rc of the update; otherwise -1
+  // (nothing launched: the Python side converts them first). All checks are
+  // C++ attribute reads, no tensor is made.
+  int update_any(const at::Tensor& idx, const at::Tensor& td) {
+    if (!idx.is_cuda() || !td.is_cuda() || idx.get_device() != device_ ||
+        td.get_device() != device_ || idx.scalar_type() != at::kLong ||
+        td.scalar_type() != at::kFloat || !idx.is_contiguous() || !td.is_contiguous() ||
+        idx.numel() != td.numel() || idx.numel() == 0)
+      return -1;
+    c10::cuda::CUDAGuard guard(device_);
+    return per_update_priorities(store_, idx.data_ptr<int64_t>(), td.data_ptr<float>(),
+                                 idx.numel(), stream());
+  }
+
   // update(idx int64, td float32), both contiguous on the device -> rc
   int update(const at::Tensor& idx, const at::Tensor& td) {
     c10::cuda::CUDAGuard guard(device_);
@@ -159,6 +175,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("sample_into", &Engine::sample_into)
       .def("sample_from", &Engine::sample_from)
       .def("update", &Engine::update)
+      .def("update_any", &Engine::update_any)
       .def("sample_sharded_p2p", &Engine::sample_sharded_p2p)
       .def("sample_sharded_p2p_into", &Engine::sample_sharded_p2p_into)
       .def("update_shard_count", &Engine::update_shard_count);

@@ -269,6 +269,14 @@ class PERBuffer:
 
     # --------------------------------------------------------------- update
     def update_priorities(self, indices: torch.Tensor, td_errors: torch.Tensor) -> None:
+        if self._engine is not None:
+            # the common case (int64 indices, float32 TD errors, contiguous, on
+            # this device) is checked and launched in one C++ call
+            rc = self._engine.update_any(indices, td_errors)
+            if rc == 0:
+                return
+            if rc > 0:
+                _lib.check("per_update_priorities", rc)
         td = td_errors.detach() if td_errors.requires_grad else td_errors
         if td.dim() != 1:
             td = td.reshape(-1)
