@@ -456,10 +456,12 @@ def e2e_loop(buf, steps, warmup, world, seed=9):
 
 
 # ---------------------------------------------------------------- sharded
-def make_sharded(device, rank, world, total_capacity, priorities, seed=1, exchange="auto"):
+def make_sharded(device, rank, world, total_capacity, priorities, seed=1, exchange="auto",
+                 normalize="global"):
     from per_b200.sharded import ShardedPERBuffer
 
-    sb = ShardedPERBuffer(total_capacity, FIELDS_74, device=device, seed=seed, exchange=exchange)
+    sb = ShardedPERBuffer(total_capacity, FIELDS_74, device=device, seed=seed, exchange=exchange,
+                          normalize=normalize)
     cap = sb.shard_capacity
     buf = sb.shard.buf
     g = torch.Generator(device=device).manual_seed(1000 + rank)
@@ -572,8 +574,10 @@ def sharded_e2e(sb, gb, rounds, steps, warmup, world, with_add):
     return e_ms, h_td.numel() * 4 + (ROW_DIM * 4 if with_add else 0), rounds * gb * (ROW_DIM * 4 + 12)
 
 
-def sharded_measure(args, world, rank, local, big):
+def sharded_measure(args, world, rank, local, big, normalize="global"):
     """The sharded buffer across the ranks (collective; rank 0 gets the dict).
+
+    normalize="rank": weights divided by each rank's own max (no max exchange).
 
     big: 64,000,000 x 74 slots split over the ranks (lognormal(0,1)
     priorities), one step = sample of a global batch of 65,536 -> update of
@@ -583,7 +587,7 @@ def sharded_measure(args, world, rank, local, big):
     dev = torch.device("cuda", local)
     total_cap = 64_000_000 if big else CAPACITY * world
     sb = make_sharded(dev, rank, world, total_cap, "lognormal" if big else "absnormal",
-                      exchange=args.exchange)
+                      exchange=args.exchange, normalize=normalize)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     gb = 65_536 if big else BATCH * world
     rounds = 1 if big else ROUNDS
@@ -601,9 +605,15 @@ def sharded_measure(args, world, rank, local, big):
         fn = lambda: sharded_utd_step(sb, row, td, world)  # noqa: E731
         launches = 1 + ROUNDS * per_round
     per_step = gb * rounds
-    exchange_desc = ("shard totals and max weight exchanged inside the sample kernel over "
-                     "NVLink peer memory (CUDA IPC mailboxes)" if p2p else
-                     "NCCL all-gather of shard totals + all-reduce max per sample")
+    if normalize == "rank":
+        exchange_desc = ("shard totals exchanged inside the sample kernel over NVLink peer "
+                         "memory (CUDA IPC mailboxes); weights over each rank's own max"
+                         if p2p else "NCCL all-gather of shard totals per sample; weights "
+                         "over each rank's own max")
+    else:
+        exchange_desc = ("shard totals and max weight exchanged inside the sample kernel over "
+                         "NVLink peer memory (CUDA IPC mailboxes)" if p2p else
+                         "NCCL all-gather of shard totals + all-reduce max per sample")
     for _ in range(max(args.warmup, 3)):
         fn()
     torch.cuda.synchronize()
@@ -673,6 +683,12 @@ def run_sharded(args, world, rank, local):
     big_only = args.workload == "sharded64m"
     main_ = sharded_measure(args, world, rank, local, big=big_only)
     big = main_ if big_only else sharded_measure(args, world, rank, local, big=True)
+    # the opt-in rank-local normalisation, reported beside the exact global one
+    rank_norm = None
+    if world > 1 and not args.no_rank_norm:
+        rank_norm = (sharded_measure(args, world, rank, local, big=big_only, normalize="rank"),
+                     None if big_only else
+                     sharded_measure(args, world, rank, local, big=True, normalize="rank"))
     if rank == 0:
         line = {
             "metric": METRIC, "value": main_["value"], "unit": UNIT, "n_gpus": world,
@@ -688,6 +704,14 @@ def run_sharded(args, world, rank, local):
             "sharded64m": {k: big[k] for k in ("value", "ms_per_step", "e2e", "parallelism",
                                                "timing", "global_batch", "capacity_total")},
         }
+        if rank_norm is not None:
+            keys = ("value", "ms_per_step", "e2e", "parallelism")
+            line["rank_normalized"] = {
+                "weights": "each rank's weights divided by that rank's largest weight "
+                           "(ShardedPERBuffer(normalize='rank')); draws and rows unchanged",
+                **{k: rank_norm[0][k] for k in keys}}
+            if rank_norm[1] is not None:
+                line["rank_normalized"]["sharded64m"] = {k: rank_norm[1][k] for k in keys}
         print(json.dumps(line), flush=True)
 
 
@@ -973,6 +997,8 @@ def main():
                     help="skip the replay-share profile of the N=1 line")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the sharded 64M x 74 configuration of the N=1 line")
+    ap.add_argument("--no-rank-norm", action="store_true",
+                    help="N>1: skip the rank-normalised sharded measurements")
     ap.add_argument("--workload", default="utd", choices=["utd", "sharded64m"])
     ap.add_argument("--exchange", default="auto", choices=["auto", "p2p", "nccl"],
                     help="sharded mode: in-kernel peer-memory exchange or NCCL collectives")

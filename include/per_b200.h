@@ -54,7 +54,7 @@ extern "C" {
 #define PER_MAX_GRID 4096  /* max CTAs of one grid-synchronised launch */
 #define PER_SCRATCH_BYTES (256 + 4 * PER_MAX_GRID)
 #define PER_MAX_SHARDS 64  /* shards of one sharded buffer */
-#define PER_MAILBOX_BYTES 4096  /* peer-memory mailbox of one rank */
+#define PER_MAILBOX_BYTES 8192  /* peer-memory mailbox of one rank */
 #define PER_IPC_HANDLE_BYTES 64
 
 /* return codes */
@@ -276,6 +276,21 @@ int per_sample_sharded_p2p_rng(const per_store_t* store, int32_t rank, int32_t w
                                uint64_t* counter, int64_t batch, float beta, float* out,
                                int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
                                int64_t* count, void* stream);
+
+/* per_sample_sharded_p2p_rng() with each rank's weights normalised by the
+ * largest weight among the draws that rank owns, instead of the largest of
+ * the whole global batch: the second exchange (the max weight, one more
+ * NVLink round trip per call) is left out. Indices, rows and the unnormalised
+ * weights are those of per_sample_sharded_p2p_rng(); only the scale of each
+ * rank's weights differs (a per-rank constant), as when each rank normalises
+ * its own batch. No counterpart in the reference (single GPU; buffer.py:92
+ * normalises by the batch max). Ranks may run one call apart; the mailbox
+ * keeps the statistics of two consecutive calls. */
+int per_sample_sharded_p2p_local_rng(const per_store_t* store, int32_t rank, int32_t world,
+                                     int64_t shard_base, void* const* mailboxes, uint64_t seed,
+                                     uint64_t* counter, int64_t batch, float beta, float* out,
+                                     int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
+                                     int64_t* count, void* stream);
 
 /* Largest batch per_sample_sharded_p2p() accepts for this store on the
  * current device (one wave of co-resident CTAs, one tile per warp). */

@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cap, q):
+def _worker(rank, world, port, cap, q, normalize="global"):
     for p in (os.path.dirname(HERE), os.path.join(os.path.dirname(HERE), "triton-per_b200"), HERE):
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -46,7 +46,7 @@ def _worker(rank, world, port, cap, q):
         all_leaves = rng.lognormal(0, 1, shard_cap * world).astype(np.float32)
         rows = np.arange(shard_cap * world * 2, dtype=np.float32).reshape(-1, 2)
         shard = CpuShard(shard_cap, fields)
-        buf = ShardedPERBuffer(cap, fields, device="cpu", seed=3, shard=shard)
+        buf = ShardedPERBuffer(cap, fields, device="cpu", seed=3, shard=shard, normalize=normalize)
         lo = rank * shard_cap
         buf.add({"x": torch.from_numpy(rows[lo: lo + shard_cap])})
         shard.set_leaves(all_leaves[lo: lo + shard_cap])
@@ -70,12 +70,16 @@ def _worker(rank, world, port, cap, q):
         dist.destroy_process_group()
 
 
-def test_sharded_union_equals_single_buffer():
+@pytest.mark.parametrize("normalize", ["global", "rank"])
+def test_sharded_union_equals_single_buffer(normalize):
+    """normalize="rank": the same draws, each rank's weights divided by their
+    largest value on that rank (no max all-reduce)."""
     world, cap = 2, 6000
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cap, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cap, q, normalize))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]
@@ -104,7 +108,12 @@ def test_sharded_union_equals_single_buffer():
     eq, exc, bad = oracle.classify_indices(idx_g, idx_o, rand, csum, total_cap)
     assert bad.size == 0 and exc <= 40
     w_ref = oracle.weights_for(lv, csum[-1], total_cap, idx_g, 0.4)
-    np.testing.assert_allclose(w_g, w_ref, rtol=1e-5)
+    if normalize == "global":
+        np.testing.assert_allclose(w_g, w_ref, rtol=1e-5)
+    else:
+        for rank, (idx, w, pos, x), *_ in results:
+            assert w.max() == 1.0
+            np.testing.assert_allclose(w, w_ref[pos] / w_ref[pos].max(), rtol=1e-5)
 
     # routed update: every shard equals the oracle's update of the whole store
     st = oracle.OracleStore(total_cap, {"x": 2})

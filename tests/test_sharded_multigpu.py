@@ -5,6 +5,8 @@ in-kernel uniforms on every rank. Both exchanges are run:
 NCCL collectives between kernels, and the in-kernel exchange over peer
 memory (several calls in a row, so the mailboxes' sequence numbers advance,
 and one batch above the one-wave limit, which takes the collective path).
+With normalize="rank" the draws and rows are the same and each rank's weights
+are the global ones divided by their largest value on that rank.
 Skipped with fewer GPUs than ranks."""
 
 import os
@@ -27,7 +29,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q, exchange):
+def _worker(rank, world, port, q, exchange, normalize="global"):
     for p in (os.path.dirname(HERE), os.path.join(os.path.dirname(HERE), "triton-per_b200"), HERE):
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -49,7 +51,8 @@ def _worker(rank, world, port, q, exchange):
         total = shard_cap * world
         leaves = rng.lognormal(0, 1, total).astype(np.float32)
         rows = rng.standard_normal((total, 6), dtype=np.float32)
-        buf = ShardedPERBuffer(total, {"x": 6}, device=f"cuda:{rank}", seed=9, exchange=exchange)
+        buf = ShardedPERBuffer(total, {"x": 6}, device=f"cuda:{rank}", seed=9, exchange=exchange,
+                               normalize=normalize)
         assert buf.exchange == exchange
         lo = rank * shard_cap
         b = buf.shard.buf
@@ -90,15 +93,16 @@ def _worker(rank, world, port, q, exchange):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+@pytest.mark.parametrize("exchange,normalize",
+                         [("nccl", "global"), ("p2p", "global"), ("p2p", "rank"), ("nccl", "rank")])
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_sharded_across_gpus(exchange):
+def test_sharded_across_gpus(exchange, normalize):
     from oracle import oracle
 
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, q, exchange)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, q, exchange, normalize)) for r in range(WORLD)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(WORLD)]
@@ -126,8 +130,15 @@ def test_sharded_across_gpus(exchange):
         assert (idx_g >= 0).all()
         _, exc, bad = oracle.classify_indices(idx_g, idx_o, rand, csum, total)
         assert bad.size == 0
-        np.testing.assert_allclose(w_g, oracle.weights_for(lv, csum[-1], total, idx_g, 0.5),
-                                   rtol=1e-6)
+        w_o = oracle.weights_for(lv, csum[-1], total, idx_g, 0.5)
+        if normalize == "global":
+            np.testing.assert_allclose(w_g, w_o, rtol=1e-6)
+        else:  # each rank's weights over its own largest one
+            for rank, draws, *_ in results:
+                pos = draws[k][3]
+                if pos.size:
+                    assert draws[k][2].max() == 1.0
+                    np.testing.assert_allclose(draws[k][2], w_o[pos] / w_o[pos].max(), rtol=2e-6)
     st = oracle.OracleStore(total, {"x": 6})
     st.set_priorities(lv)
     for rank, _, upd_idx, upd_td, *_ in results:

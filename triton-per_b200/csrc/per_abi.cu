@@ -325,7 +325,7 @@ int sample_sharded(const per_store_t* store, int32_t rank, int32_t world, int64_
 int sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world, int64_t shard_base,
                        void* const* mailboxes, const float* rand, const PerRng* rng, int64_t batch,
                        float beta, float* out, int64_t out_stride, int64_t* idx, float* w,
-                       int32_t* pos, int64_t* count, void* stream) {
+                       int32_t* pos, int64_t* count, int32_t local_norm, void* stream) {
   int rc = check_store(store);
   if (rc) return rc;
   if (!mailboxes || (!rand && !rng) || !out || !idx || !w || !pos || !count)
@@ -344,7 +344,7 @@ int sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world, in
     return PER_ERR_MISALIGNED;
   return per_launch_sample_sharded_p2p(tree_of(store), rank, world, shard_base,
                                        reinterpret_cast<PerMailbox* const*>(mailboxes), rand, rng,
-                                       batch, beta, out, ow, idx, w, pos, count,
+                                       batch, beta, out, ow, idx, w, pos, count, local_norm,
                                        (cudaStream_t)stream);
 }
 
@@ -481,7 +481,7 @@ int per_sample_sharded_p2p(const per_store_t* store, int32_t rank, int32_t world
   PerRange range("per_sample_sharded_p2p");
   if (!rand) return PER_ERR_NULL_POINTER;
   return sample_sharded_p2p(store, rank, world, shard_base, mailboxes, rand, nullptr, batch, beta,
-                            out, out_stride, idx, w, pos, count, stream);
+                            out, out_stride, idx, w, pos, count, 0, stream);
 }
 
 int per_sample_sharded_p2p_rng(const per_store_t* store, int32_t rank, int32_t world,
@@ -492,7 +492,18 @@ int per_sample_sharded_p2p_rng(const per_store_t* store, int32_t rank, int32_t w
   PerRange range("per_sample_sharded_p2p_rng");
   const PerRng rng{(unsigned long long)seed, reinterpret_cast<unsigned long long*>(counter)};
   return sample_sharded_p2p(store, rank, world, shard_base, mailboxes, nullptr, &rng, batch, beta,
-                            out, out_stride, idx, w, pos, count, stream);
+                            out, out_stride, idx, w, pos, count, 0, stream);
+}
+
+int per_sample_sharded_p2p_local_rng(const per_store_t* store, int32_t rank, int32_t world,
+                                     int64_t shard_base, void* const* mailboxes, uint64_t seed,
+                                     uint64_t* counter, int64_t batch, float beta, float* out,
+                                     int64_t out_stride, int64_t* idx, float* w, int32_t* pos,
+                                     int64_t* count, void* stream) {
+  PerRange range("per_sample_sharded_p2p_local_rng");
+  const PerRng rng{(unsigned long long)seed, reinterpret_cast<unsigned long long*>(counter)};
+  return sample_sharded_p2p(store, rank, world, shard_base, mailboxes, nullptr, &rng, batch, beta,
+                            out, out_stride, idx, w, pos, count, 1, stream);
 }
 
 int per_sample_sharded_p2p_max_batch(const per_store_t* store, int64_t* max_batch) {

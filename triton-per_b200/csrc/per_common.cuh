@@ -45,7 +45,10 @@ static_assert(sizeof(PerScratch) == PER_SCRATCH_BYTES, "scratch layout");
 struct PerMailbox {
   unsigned long long seq;  // sample calls completed by the owning rank (local)
   unsigned long long pad0[15];
-  unsigned long long stats[PER_MAX_SHARDS][4];  // slot g: total (2 halves), size (2 halves)
+  // slot g of call parity p: total (2 halves), size (2 halves); two parities,
+  // because without the max exchange a peer may publish call k+1 while this
+  // rank still reads call k
+  unsigned long long stats[2][PER_MAX_SHARDS][4];
   unsigned long long max_w[PER_MAX_SHARDS];     // slot g: max weight bits
 };
 static_assert(sizeof(PerMailbox) <= PER_MAILBOX_BYTES, "mailbox layout");

@@ -67,6 +67,7 @@ int per_launch_sample_sharded_p2p(const PerTree& t, int32_t rank, int32_t world,
                                   int64_t shard_base, PerMailbox* const* mailboxes,
                                   const float* rand, const PerRng* rng, int64_t batch, float beta,
                                   float* out, int64_t out_stride, int64_t* idx, float* w,
-                                  int32_t* pos, int64_t* count, cudaStream_t stream);
+                                  int32_t* pos, int64_t* count, int32_t local_norm,
+                                  cudaStream_t stream);
 int per_launch_normalize(float* w, const int64_t* count, const float* gmax, int64_t cap,
                          cudaStream_t stream);

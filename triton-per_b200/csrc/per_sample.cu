@@ -85,6 +85,7 @@ struct SampleArgs {
   float* local_max;              // max unnormalised weight over this shard's draws
   PerMailbox* const* mailboxes;  // exchange over peer memory: every rank's mailbox
   int32_t p2p;                   // 1: exchange stats and max in-kernel through the mailboxes
+  int32_t local_norm;            // p2p: weights normalised by this rank's max (no max exchange)
   // sharded, in-kernel exchange: each CTA routes its slice of `slice` global
   // draws first and searches only the draws this shard owns
   int32_t owned_only;
@@ -631,7 +632,7 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
         const unsigned long long sb = (unsigned long long)__double_as_longlong(szd);
         for (int g = lane; g < a.world; g += 32) {
           if (g == a.rank) continue;  // every CTA of this rank has its own values
-          unsigned long long* slot = (g < 32 ? peer_lo : peer_hi)->stats[a.rank];
+          unsigned long long* slot = (g < 32 ? peer_lo : peer_hi)->stats[s_seq & 1ull][a.rank];
           per_mail_put(slot + 0, (uint32_t)tb, tag);
           per_mail_put(slot + 1, (uint32_t)(tb >> 32), tag);
           per_mail_put(slot + 2, (uint32_t)sb, tag);
@@ -645,7 +646,7 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
           continue;
         }
         uint32_t d[4] = {0u, 0u, 0u, 0u};
-        per_mail_get(mine->stats[g], 4, tag, d, t.status);
+        per_mail_get(mine->stats[s_seq & 1ull][g], 4, tag, d, t.status);
         s_stats[g][0] = __longlong_as_double((long long)(((unsigned long long)d[1] << 32) | d[0]));
         s_stats[g][1] = __longlong_as_double((long long)(((unsigned long long)d[3] << 32) | d[2]));
       }
@@ -760,7 +761,11 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
       }
     }
     __syncwarp();
-    if (SHARDED && a.p2p) {
+    if (SHARDED && a.p2p && a.local_norm) {
+      // weights normalised by this rank's max (no exchange): record the call
+      if (lane == 0 && blockIdx.x == 0) *(volatile unsigned long long*)&s_mine->seq = s_seq;
+      __syncwarp();
+    } else if (SHARDED && a.p2p) {
       // ---- max weight over all ranks: CTA 0 publishes this rank's max into
       // every mailbox, every CTA reduces the slots of its own mailbox
       const float lmax = s_gmax;
@@ -1438,6 +1443,7 @@ void fill_common(SampleArgs& a, const PerTree& t, const float* rand, int64_t bat
   a.local_max = nullptr;
   a.mailboxes = nullptr;
   a.p2p = 0;
+  a.local_norm = 0;
   a.owned_only = 0;
   a.slice = 0;
   a.use_rng = 0;
@@ -1620,7 +1626,8 @@ int per_launch_sample_sharded_p2p(const PerTree& t, int32_t rank, int32_t world,
                                   int64_t shard_base, PerMailbox* const* mailboxes,
                                   const float* rand, const PerRng* rng, int64_t batch, float beta,
                                   float* out, int64_t out_stride, int64_t* idx, float* w,
-                                  int32_t* pos, int64_t* count, cudaStream_t stream) {
+                                  int32_t* pos, int64_t* count, int32_t local_norm,
+                                  cudaStream_t stream) {
   SampleArgs a;
   fill_common(a, t, rand, batch, beta, out, out_stride, idx, w);
   a.rank = rank;
@@ -1630,6 +1637,7 @@ int per_launch_sample_sharded_p2p(const PerTree& t, int32_t rank, int32_t world,
   a.count = reinterpret_cast<unsigned long long*>(count);
   a.mailboxes = mailboxes;
   a.p2p = 1;
+  a.local_norm = local_norm ? 1 : 0;
   a.owned_only = 1;
   set_rng(a, rng);
   return launch_any<true>(a, vec_width(t, out, out_stride), stream);

@@ -70,8 +70,10 @@ class Engine {
 
   // sharded sample with the in-kernel exchange and uniforms:
   // -> (rc, views, idx, w, pos, count) of this rank's owned draws
+  // local: weights normalised by this rank's own max (no max exchange)
   py::tuple sample_sharded_p2p(int32_t rank, int32_t world, int64_t shard_base, int64_t mailboxes,
-                               int64_t batch, double beta, uint64_t seed, int64_t counter) {
+                               int64_t batch, double beta, uint64_t seed, int64_t counter,
+                               bool local) {
     c10::cuda::CUDAGuard guard(device_);
     const auto f = at::TensorOptions().dtype(at::kFloat).device(at::kCUDA, device_);
     at::Tensor out = at::empty({batch, row_dim_}, f.dtype(row_dtype_));
@@ -79,7 +81,7 @@ class Engine {
     at::Tensor w = at::empty({batch}, f);
     at::Tensor pos = at::empty({batch}, f.dtype(at::kInt));
     at::Tensor idx = ic.narrow(0, 0, batch), count = ic.narrow(0, batch, 1);
-    const int rc = per_sample_sharded_p2p_rng(
+    const int rc = (local ? per_sample_sharded_p2p_local_rng : per_sample_sharded_p2p_rng)(
         store_, rank, world, shard_base, reinterpret_cast<void* const*>(mailboxes), seed,
         reinterpret_cast<uint64_t*>(counter), batch, static_cast<float>(beta),
         rows(out), row_dim_, idx.data_ptr<int64_t>(), w.data_ptr<float>(),
@@ -92,9 +94,9 @@ class Engine {
   int sample_sharded_p2p_into(int32_t rank, int32_t world, int64_t shard_base, int64_t mailboxes,
                               int64_t batch, double beta, uint64_t seed, int64_t counter,
                               int64_t rows_ptr, int64_t row_stride, int64_t idx, int64_t w,
-                              int64_t pos, int64_t count) {
+                              int64_t pos, int64_t count, bool local) {
     c10::cuda::CUDAGuard guard(device_);
-    return per_sample_sharded_p2p_rng(
+    return (local ? per_sample_sharded_p2p_local_rng : per_sample_sharded_p2p_rng)(
         store_, rank, world, shard_base, reinterpret_cast<void* const*>(mailboxes), seed,
         reinterpret_cast<uint64_t*>(counter), batch, static_cast<float>(beta),
         reinterpret_cast<float*>(rows_ptr), row_stride, reinterpret_cast<int64_t*>(idx),

@@ -105,6 +105,9 @@ SIGNATURES = {
                                               ctypes.c_float, vp, i64, vp, vp, vp, vp, vp, vp]),
     "per_sample_sharded_p2p_rng": (ctypes.c_int, [ctypes.POINTER(Store), i32, i32, i64, vp, u64, vp,
                                                   i64, ctypes.c_float, vp, i64, vp, vp, vp, vp, vp]),
+    "per_sample_sharded_p2p_local_rng": (ctypes.c_int, [ctypes.POINTER(Store), i32, i32, i64, vp, u64,
+                                                        vp, i64, ctypes.c_float, vp, i64, vp, vp, vp,
+                                                        vp, vp]),
     "per_sample_sharded_p2p_max_batch": (ctypes.c_int, [ctypes.POINTER(Store), vp]),
     "per_mailbox_create": (ctypes.c_int, [ctypes.POINTER(vp), vp]),
     "per_mailbox_open": (ctypes.c_int, [vp, ctypes.POINTER(vp)]),

@@ -28,6 +28,13 @@ The two exchanges run one of two ways:
 - collectives (`exchange="nccl"`, and larger batches): stats kernel,
   all-gather, sample kernel, all-reduce MAX, normalise kernel.
 
+normalize="rank" normalises each rank's weights by the largest weight among
+the draws that rank owns (a per-rank constant factor on the global-max
+weights; the draws, rows and relative weights are unchanged). It leaves out
+the max exchange, so the in-kernel path crosses NVLink once per sample
+instead of twice, and the collective path skips its all-reduce. The default,
+normalize="global", keeps the single-buffer weights exactly.
+
 update_priorities(idx, td) applies the entries whose global index this rank
 owns (the data-parallel case: every rank updates the draws it sampled); with
 route=True every rank's entries are all-gathered first, so a rank may update
@@ -126,28 +133,34 @@ class CudaShard:
                     lmax.data_ptr(), _stream_ptr(dev)))
         return out, idx, w, pos, count, lmax
 
-    def sample_p2p_into(self, rank, world, base, mailboxes, beta, rng, out: ShardSampleOut):
+    def sample_p2p_into(self, rank, world, base, mailboxes, beta, rng, out: ShardSampleOut,
+                        local: bool = False):
         """sample_p2p with in-kernel uniforms into a caller-owned destination."""
         buf = self.buf
         args = (rank, world, base, mailboxes.data_ptr(), out.batch, float(beta), rng[0],
                 rng[1].data_ptr(), out.rows.data_ptr(), out.rows.stride(0), out.idx.data_ptr(),
                 out.w.data_ptr(), out.pos.data_ptr(), out.count.data_ptr())
+        name = "per_sample_sharded_p2p_local_rng" if local else "per_sample_sharded_p2p_rng"
         if buf._engine is not None:
-            rc = buf._engine.sample_sharded_p2p_into(*args)
+            rc = buf._engine.sample_sharded_p2p_into(*args, bool(local))
             if rc:
-                _lib.check("per_sample_sharded_p2p_rng", rc)
+                _lib.check(name, rc)
         else:
-            buf._call("per_sample_sharded_p2p_rng", _lib.lib.per_sample_sharded_p2p_rng,
+            buf._call(name, getattr(_lib.lib, name),
                       buf._store_ref, args[0], args[1], args[2], args[3], args[6], args[7],
                       args[4], args[5], args[8], args[9], args[10], args[11], args[12], args[13])
 
-    def sample_p2p(self, rank, world, base, mailboxes, rand, beta, rng=None, batch=None):
+    def sample_p2p(self, rank, world, base, mailboxes, rand, beta, rng=None, batch=None,
+                   local: bool = False):
+        """local (in-kernel uniforms only): weights normalised by this rank's max."""
         b = rand.numel() if rng is None else batch
         buf = self.buf
+        if local and rng is None:
+            raise ValueError("rank-local normalisation needs the in-kernel uniforms")
         if rng is not None and buf._engine is not None:
             rc, views, idx, w, pos, count = buf._engine.sample_sharded_p2p(
                 rank, world, base, mailboxes.data_ptr(), b, float(beta), rng[0],
-                rng[1].data_ptr())
+                rng[1].data_ptr(), bool(local))
             if rc:
                 _lib.check("per_sample_sharded_p2p_rng", rc)
             return views, idx, w, pos, count
@@ -161,7 +174,8 @@ class CudaShard:
                       out.data_ptr(), buf.row_dim, idx.data_ptr(), w.data_ptr(), pos.data_ptr(),
                       count.data_ptr())
         else:
-            buf._call("per_sample_sharded_p2p_rng", _lib.lib.per_sample_sharded_p2p_rng,
+            name = "per_sample_sharded_p2p_local_rng" if local else "per_sample_sharded_p2p_rng"
+            buf._call(name, getattr(_lib.lib, name),
                       buf._store_ref, rank, world, base, mailboxes.data_ptr(), rng[0],
                       rng[1].data_ptr(), b, float(beta), out.data_ptr(), buf.row_dim,
                       idx.data_ptr(), w.data_ptr(), pos.data_ptr(), count.data_ptr())
@@ -206,9 +220,13 @@ class ShardedPERBuffer:
         seed: int = 0,
         shard=None,
         exchange: str = "auto",
+        normalize: str = "global",
     ):
         if exchange not in ("auto", "p2p", "nccl"):
             raise ValueError(f"exchange must be 'auto', 'p2p' or 'nccl', not {exchange!r}")
+        if normalize not in ("global", "rank"):
+            raise ValueError(f"normalize must be 'global' or 'rank', not {normalize!r}")
+        self.normalize = normalize
         self.group = group
         distributed = dist.is_available() and dist.is_initialized()
         self.rank = dist.get_rank(group) if distributed else 0
@@ -371,7 +389,8 @@ class ShardedPERBuffer:
                 raise ValueError("sample(out=) needs the in-kernel exchange and a batch of at "
                                  f"most p2p_max_batch ({self.p2p_max_batch})")
             self.shard.sample_p2p_into(self.rank, self.world, self.base, self._mailboxes, beta,
-                                       (self.seed, self._rng_counter), out)
+                                       (self.seed, self._rng_counter), out,
+                                       local=self.normalize == "rank")
             self._last = (out.idx, out.count)
             return ShardSample(out.views, out.idx, out.w, out.count, out.pos)
         if not isinstance(self.shard, CudaShard):
@@ -380,7 +399,8 @@ class ShardedPERBuffer:
         rng = (self.seed, self._rng_counter)
         if self.exchange == "p2p" and batch_size <= self.p2p_max_batch:
             out, idx, w, pos, count = self.shard.sample_p2p(
-                self.rank, self.world, self.base, self._mailboxes, None, beta, rng, batch_size)
+                self.rank, self.world, self.base, self._mailboxes, None, beta, rng, batch_size,
+                local=self.normalize == "rank")
             self._last = (idx, count)
             views = out if isinstance(out, dict) else self._views(out)
             return ShardSample(views, idx, w, count, pos)
@@ -388,7 +408,7 @@ class ShardedPERBuffer:
             self._exchange_stats()
             out, idx, w, pos, count, lmax = self.shard.sample(
                 self.rank, self.world, self.base, self._all_stats, None, beta, rng, batch_size)
-            if self.world > 1:
+            if self.world > 1 and self.normalize == "global":
                 dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
             self.shard.normalize(w, count, lmax)
         self._last = (idx, count)
@@ -400,7 +420,8 @@ class ShardedPERBuffer:
     def sample_from_uniforms(self, rand: torch.Tensor, beta: float = 0.4) -> ShardSample:
         """sample() with caller-provided global uniforms (identical on every rank)."""
         rand = rand.to(device=self.device, dtype=torch.float32).contiguous()
-        if self.exchange == "p2p" and rand.numel() <= self.p2p_max_batch:
+        if self.exchange == "p2p" and rand.numel() <= self.p2p_max_batch and \
+                self.normalize == "global":
             out, idx, w, pos, count = self.shard.sample_p2p(
                 self.rank, self.world, self.base, self._mailboxes, rand, beta)
             views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
@@ -408,7 +429,7 @@ class ShardedPERBuffer:
         self._exchange_stats()
         out, idx, w, pos, count, lmax = self.shard.sample(
             self.rank, self.world, self.base, self._all_stats, rand, beta)
-        if self.world > 1:
+        if self.world > 1 and self.normalize == "global":
             dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
         self.shard.normalize(w, count, lmax)
         views = {name: out[:, a:b] for name, (a, b) in self._offsets.items()}
