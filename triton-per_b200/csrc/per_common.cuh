@@ -425,6 +425,12 @@ __device__ __forceinline__ void per_tma_gather4(void* sdst, const void* tmap, in
       : "memory");
 }
 
+// Bring a tensor map (a kernel parameter or global memory) into the
+// descriptor cache ahead of its first copy.
+__device__ __forceinline__ void per_prefetch_tensormap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
 // Bulk copy global -> this CTA's shared memory, completing on `bar`.
 // Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void per_bulk_load(void* sdst, const void* gsrc, uint32_t bytes,

@@ -251,12 +251,15 @@ __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stag
                                            int gpitch, int64_t j0, int rn, int lane) {
   using V = typename VecT<VEC>::T;
   const int nvec = a.nvec;
-  const V* sv = reinterpret_cast<const V*>(stage);
-  V* dst = reinterpret_cast<V*>(a.out) + j0 * (a.out_stride / VEC);
+  // the tile and the output never overlap: the loads of later pieces may go
+  // out before the stores of earlier ones
+  const V* __restrict__ sv = reinterpret_cast<const V*>(stage);
+  V* __restrict__ dst = reinterpret_cast<V*>(a.out) + j0 * (a.out_stride / VEC);
   const int dstride = (int)(a.out_stride / VEC);
   if (nvec >= 32) {  // at most one row wrap per step of 32
     const int pieces = rn * nvec;
     int r = 0, c = lane;
+#pragma unroll 4
     for (int p = lane; p < pieces; p += 32) {
       dst[r * dstride + c] = sv[(r >> 2) * gpitch + (r & 3) * spitch + c];
       c += 32;
@@ -280,10 +283,11 @@ __device__ __forceinline__ void store_rows(const SampleArgs& a, const void* stag
 // (any 4-byte alignment; lower latency when an SM has only a few rows).
 __device__ __forceinline__ void gather_issue(const SampleArgs& a, unsigned char* stage,
                                              const int32_t* s_idx, int r0, int rn, int lane,
-                                             uint64_t* mbar, bool g4, const void* tmap) {
+                                             uint64_t* mbar, bool g4, const void* tmap,
+                                             bool fence = true) {
   if (g4) {
     const int ng = (rn + 3) >> 2;
-    per_fence_proxy_async_smem();  // earlier generic accesses of the tile before the copies
+    if (fence) per_fence_proxy_async_smem();  // earlier generic accesses of the tile before the copies
     __syncwarp();
     if (lane == 0) per_mbar_arrive_expect_tx(mbar, (uint32_t)(ng * 4 * a.row_bytes));
     __syncwarp();
@@ -867,6 +871,9 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     }
   }
 
+  // the warp's tile was written only by the level-line copies (generic
+  // proxy, completed, read back) before its first gather: no proxy fence then
+  bool first_tile = true;
   for (; tile < ntiles; tile += tstep) {
     const bool last_tile = tile + tstep >= ntiles;
     const int64_t wj0 = tile * tile_draws + warp * D;  // first draw of this warp
@@ -1005,7 +1012,9 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     __syncwarp();
     const int rps = a.rows_per_stage;
     if (rps > 0 && nrows > 0)
-      gather_issue(a, stage, s_rows[warp], 0, min(rps, nrows), lane, &s_mbar[warp], g4, &rows_map);
+      gather_issue(a, stage, s_rows[warp], 0, min(rps, nrows), lane, &s_mbar[warp], g4, &rows_map,
+                   !first_tile);
+    first_tile = false;
 
     float wv = 0.f;
     if (own) {
@@ -1076,10 +1085,16 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     return;
   }
   const float gmax = s_gmax;
-  for (int64_t tl = blockIdx.x; tl < a.num_tiles; tl += gridDim.x) {
+  // earlier tiles' weights were stored unnormalised; the last tile's are in
+  // registers (no load on the common one-tile path)
+  int64_t tl = blockIdx.x;
+  for (; tl + gridDim.x < a.num_tiles; tl += gridDim.x) {
     const int64_t j = tl * tile_draws + warp * D + lane;
-    const bool last = tl + gridDim.x >= a.num_tiles;
-    if (lane < D && j < a.batch) a.w[j] = __fdiv_rn(last ? w_last : a.w[j], gmax);
+    if (lane < D && j < a.batch) a.w[j] = __fdiv_rn(a.w[j], gmax);
+  }
+  if (tl < a.num_tiles) {
+    const int64_t j = tl * tile_draws + warp * D + lane;
+    if (lane < D && j < a.batch) a.w[j] = __fdiv_rn(w_last, gmax);
   }
   if constexpr (WIDE) bulk_wait_all();  // the last row stores are complete before the CTA exits
 }
