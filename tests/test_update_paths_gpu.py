@@ -1,6 +1,9 @@
 """The update paths against the oracle (B200).
 
-Batches up to a few thousand indices go through the one-CTA prefetched update
+Batches of up to 512 indices go through the partitioned update (CTAs owning
+disjoint top-level nodes, each applying its entries in rounds of 32 with warp
+elections). Batches up to a few thousand indices go through the one-CTA
+prefetched update
 in passes of up to 512 entries; a later pass overwrites an earlier one, so
 the last occurrence of a slot still wins across passes. Larger batches take
 the grid path. Every path must give the oracle's leaves (last occurrence
@@ -30,7 +33,9 @@ def _dup_batch(rng, cap, n):
     return idx.astype(np.int64), td
 
 
-@pytest.mark.parametrize("cap,n", [(1_000_000, 300), (1_000_000, 513), (1_000_000, 1024),
+@pytest.mark.parametrize("cap,n", [(1_000_000, 1), (1_000_000, 32), (1_000_000, 256),
+                                   (1_000_000, 512), (100_000, 300), (20_000, 500),
+                                   (5_000_000, 400), (1_000_000, 300), (1_000_000, 513), (1_000_000, 1024),
                                    (1_000_000, 2500), (1_000_000, 4096), (1_000_000, 5000),
                                    (5_000_000, 700), (5_000_000, 3000)])
 def test_update_matches_oracle(cap, n):
@@ -53,7 +58,8 @@ def test_update_matches_oracle(cap, n):
     assert s["errors"] == 0 and s["timeouts"] == 0
 
 
-@pytest.mark.parametrize("n,count", [(600, 250), (2048, 2048), (2048, 0), (4096, 1500)])
+@pytest.mark.parametrize("n,count", [(400, 150), (512, 512), (256, 0), (600, 250),
+                                     (2048, 2048), (2048, 0), (4096, 1500)])
 def test_shard_update_reads_only_the_counted_prefix(n, count):
     rng = np.random.default_rng(n + count)
     cap, base = 200_000, 400_000
@@ -82,3 +88,46 @@ def test_shard_update_reads_only_the_counted_prefix(n, count):
     check_tree(buf)
     s = buf.status()
     assert s["foreign"] == count // 10 and s["bad_indices"] == 0 and s["errors"] == 0
+
+
+def _apply_and_check(cap, leaves, batches):
+    buf = make_buffer(cap, {"x": 1}, None, leaves)
+    st = oracle.OracleStore(cap, {"x": 1})
+    lv = np.zeros(st.capacity_padded, np.float32)
+    lv[:cap] = leaves
+    st.set_priorities(lv)
+    for idx, td in batches:
+        buf.update_priorities(torch.from_numpy(idx).cuda(), torch.from_numpy(td).cuda())
+        st.update_priorities(idx, td)
+    np.testing.assert_allclose(buf.priorities.cpu().numpy()[:cap], st.priorities[:cap],
+                               rtol=1e-6, atol=0)
+    check_tree(buf)
+    assert buf._max_priority.item() == pytest.approx(float(st.max_priority), rel=1e-6)
+    s = buf.status()
+    assert s["errors"] == 0 and s["timeouts"] == 0
+
+
+def test_partitioned_update_one_top_node_many_rounds():
+    """512 entries under one top-level node (one CTA takes them all: 16
+    rounds of 32, duplicates across rounds): the last occurrence still wins."""
+    rng = np.random.default_rng(5)
+    cap = 1_000_000
+    leaves = cases.leaves_abs_normal(rng, cap)
+    node = 321  # top-level node of a 1M store: slots 321 * 1024 ...
+    batches = []
+    for _ in range(2):
+        idx = (node * 1024 + rng.integers(0, 1024, 512)).astype(np.int64)
+        idx[rng.integers(0, 512, 100)] = idx[rng.integers(0, 512, 100)]  # more duplicates
+        td = (rng.standard_normal(512) * 2).astype(np.float32)
+        batches.append((idx, td))
+    _apply_and_check(cap, leaves, batches)
+
+
+def test_partitioned_update_one_slot_repeated():
+    """Every entry names the same slot: the last TD error wins."""
+    rng = np.random.default_rng(6)
+    cap = 1_000_000
+    leaves = cases.leaves_abs_normal(rng, cap)
+    idx = np.full(300, 777_777, np.int64)
+    td = rng.random(300).astype(np.float32)
+    _apply_and_check(cap, leaves, [(idx, td)])

@@ -408,6 +408,198 @@ __global__ void __launch_bounds__(kThreads, 1) per_update_lines_kernel(UpdateArg
   }
 }
 
+// ---------------------------------------------------------------- partitioned update
+// Batches of up to kWMaxN indices: K one-warp CTAs, CTA k taking the entries
+// whose top-level ancestor (the node of level T above the leaf, T the highest
+// maintained level) hashes to k. Entries under different top-level nodes
+// touch disjoint nodes at every level, so the CTAs never coordinate: each
+// loads every entry, keeps its own in position order, and applies them in
+// rounds of 32 (one per lane). A round fetches every lane's line of every
+// level at once (duplicates included), elects the winner of each slot (the
+// highest lane among equal slots: the last occurrence) and the owner of each
+// touched node (the lowest lane among equal nodes) with warp matches while
+// the lines are in flight, then patches the winning leaves into their
+// owner's line and sums level by level, each owner patching its node into
+// the line of its parent's owner. Later rounds see earlier rounds' writes
+// (same warp, program order), so the last occurrence wins across rounds too.
+// Node values are per_sum32_tree of the same children as in the other update
+// paths.
+constexpr int kWMaxN = 512;              // entries of a batch
+constexpr int kWEntriesPerCta = 16;      // expected entries per CTA
+constexpr int kWMaxT = 4;                // tree levels above the leaves
+
+// Named barrier 1 between the priority warps (arrive) and warp 0 (sync).
+__device__ __forceinline__ void named_bar_arrive_upd(int count) {
+  asm volatile("bar.arrive 1, %0;" ::"r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_sync_upd(int count) {
+  asm volatile("bar.sync 1, %0;" ::"r"(count) : "memory");
+}
+
+// CTA of a top-level node among a power-of-two number of CTAs (mask kmask)
+__device__ __forceinline__ uint32_t top_cta(uint32_t top_node, uint32_t kmask) {
+  return ((top_node * 2654435761u) >> 16) & kmask;
+}
+
+// Issue (no wait) the copies of lane d's line of level L (the children of
+// its node of level L + 1) for lanes d < ra into lines d of `tile`, 4 lines
+// per instruction. Called by a whole warp.
+__device__ __forceinline__ void warp_issue_lines(const float* level, unsigned char* tile,
+                                                 uint32_t leaf, int ra, int L, int lane) {
+  const uint32_t base = per_smem_addr_generic(tile);
+  uint32_t nd[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    nd[k] = __shfl_sync(PER_FULL_MASK, leaf, (k * 32 + lane) >> 3) >> (PER_LOG_FANOUT * (L + 1));
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int q = k * 32 + lane;
+    const int d = q >> 3, part = q & 7;
+    if (d < ra)
+      per_cp_async16(base + (uint32_t)(d * PER_LINE_STRIDE + part * 16),
+                     level + (int64_t)nd[k] * PER_FANOUT + part * 4);
+  }
+}
+
+constexpr int kWPer = kWMaxN / kThreads;  // entries per thread
+
+__global__ void __launch_bounds__(kThreads) per_update_warp_kernel(UpdateArgs a) {
+  const PerTree& t = a.t;
+  const int T = t.num_levels - 1;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  __shared__ uint32_t s_leaf[kWMaxN];  // this CTA's entries in position order (slots < 2^30)
+  __shared__ float s_td[kWMaxN];
+  __shared__ float s_np[kWMaxN];       // their new priorities
+  __shared__ int s_wcnt[kWPer][kThreads / 32];
+  __shared__ __align__(16) unsigned char s_lines[kWMaxT][32 * PER_LINE_STRIDE];
+  per_wait_previous_grid();
+  int64_t li[kWPer];
+  float tv[kWPer];
+#pragma unroll
+  for (int q = 0; q < kWPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    li[q] = e < a.n ? slot_of(a, e) : -1;
+    tv[q] = e < a.n ? a.td[e] : 0.f;
+  }
+  const int64_t n = entries_of(a);
+  // this CTA's entries (those whose top-level ancestor hashes to it), in
+  // position order: warp counts, then offsets
+  const int tshift = PER_LOG_FANOUT * T;
+  const uint32_t kmask = gridDim.x - 1u;  // the launch uses a power-of-two grid
+  uint32_t nbad = 0u, nforeign = 0u;
+  bool mine[kWPer];
+  uint32_t mm[kWPer];
+#pragma unroll
+  for (int q = 0; q < kWPer; ++q) {
+    const int64_t e = threadIdx.x + q * kThreads;
+    const bool in = e < n;
+    const bool valid = in && li[q] >= 0 && li[q] < t.capacity;
+    if (in && !valid && blockIdx.x == 0) {
+      if (a.strict) ++nbad; else ++nforeign;
+    }
+    mine[q] = valid && top_cta((uint32_t)li[q] >> tshift, kmask) == blockIdx.x;
+    mm[q] = __ballot_sync(PER_FULL_MASK, mine[q]);
+    if (lane == 0) s_wcnt[q][warp] = __popc(mm[q]);
+  }
+  if (nbad) {
+    per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
+    per_flag(t.status, PER_EVT_BAD_INDEX);
+  }
+  if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
+  __syncthreads();
+  int cnt = 0;
+#pragma unroll
+  for (int q = 0; q < kWPer; ++q) {
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) {
+      if (w == warp && mine[q]) {
+        const int r = cnt + __popc(mm[q] & ((1u << lane) - 1u));
+        s_leaf[r] = (uint32_t)li[q];
+        s_td[r] = tv[q];
+      }
+      cnt += s_wcnt[q][w];
+    }
+  }
+  __syncthreads();
+  if (warp > 0) {
+    // the other warps: the new priorities of every entry of this CTA, while
+    // warp 0 fetches lines and elects
+    uint32_t tmax = 0u;
+    for (int j = threadIdx.x - 32; j < cnt; j += kThreads - 32) {
+      const float np = new_priority(t, s_td[j]);
+      s_np[j] = np;
+      tmax = max(tmax, __float_as_uint(np));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
+    if (lane == 0 && tmax) atomicMax(reinterpret_cast<unsigned int*>(t.max_priority), tmax);
+    named_bar_arrive_upd(kThreads);
+    return;
+  }
+
+  // warp 0: rounds of 32 entries (one per lane)
+  for (int r0 = 0; r0 < cnt; r0 += 32) {
+    const int ra = min(32, cnt - r0);
+    const bool act = lane < ra;
+    const uint32_t leaf = act ? s_leaf[r0 + lane] : 0u;
+#pragma unroll
+    for (int L = 0; L < kWMaxT; ++L) {
+      if (L >= T) break;
+      warp_issue_lines(t.levels[L], s_lines[L], leaf, ra, L, lane);
+    }
+    // elections while the lines are in flight (inactive lanes get keys no
+    // slot or node can have): the winner of a slot is the highest lane
+    // holding it (last occurrence), a node's owner the lowest
+    const uint32_t none = 0x80000000u | (uint32_t)lane;
+    const uint32_t msl = __match_any_sync(PER_FULL_MASK, act ? leaf : none);
+    const bool win = act && (31 - __clz(msl)) == lane;
+    int owner[kWMaxT];
+#pragma unroll
+    for (int L = 0; L < kWMaxT; ++L) {
+      owner[L] = lane;
+      if (L >= T) break;
+      const uint32_t key = act ? (leaf >> (PER_LOG_FANOUT * (L + 1))) : none;
+      owner[L] = __ffs(__match_any_sync(PER_FULL_MASK, key)) - 1;
+    }
+    if (r0 == 0) named_bar_sync_upd(kThreads);  // the new priorities are in s_np
+    const float np = act ? s_np[r0 + lane] : 0.f;
+    per_cp_async_wait_all();
+    __syncwarp();
+    // winners: leaf to the store and into the line of their chunk's owner
+    if (win) {
+      t.levels[0][leaf] = np;
+      reinterpret_cast<float*>(s_lines[0] + owner[0] * PER_LINE_STRIDE)[leaf & (PER_FANOUT - 1)] = np;
+    }
+    __syncwarp();
+    // level by level: owners sum, store, patch into the parent owner's line
+#pragma unroll
+    for (int L = 0; L < kWMaxT; ++L) {
+      if (L >= T) break;
+      if (act && owner[L] == lane) {
+        const float4* row = reinterpret_cast<const float4*>(s_lines[L] + lane * PER_LINE_STRIDE);
+        float c[32];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 v = row[k];
+          c[4 * k] = v.x;
+          c[4 * k + 1] = v.y;
+          c[4 * k + 2] = v.z;
+          c[4 * k + 3] = v.w;
+        }
+        const float v = per_sum32_tree(c);
+        const uint32_t node = leaf >> (PER_LOG_FANOUT * (L + 1));
+        t.levels[L + 1][node] = v;
+        if (L + 1 < T)
+          reinterpret_cast<float*>(s_lines[L + 1] + owner[L + 1] * PER_LINE_STRIDE)
+              [node & (PER_FANOUT - 1)] = v;
+      }
+      __syncwarp();
+    }
+  }
+  if (cnt == 0) named_bar_sync_upd(kThreads);  // the other warps' barrier completes
+}
+
 // ---------------------------------------------------------------- add
 struct AddArgs {
   PerTree t;
@@ -546,9 +738,20 @@ int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, cons
   a.base = base;
   a.strict = strict;
   a.count = reinterpret_cast<const unsigned long long*>(count);
+  const int T = t.num_levels - 1;
+  // up to kWMaxN entries: one-warp CTAs, each owning the entries under its
+  // share of the top-level nodes
+  if (n <= kWMaxN && T <= kWMaxT) {
+    const void* fw = (const void*)per_update_warp_kernel;
+    // a power of two near n / kWEntriesPerCta, at most the top level's nodes
+    int64_t k = 1;
+    while (k * kWEntriesPerCta < n && 2 * k <= t.level_len[T]) k *= 2;
+    void* args[] = {&a};
+    cudaError_t e = per_launch(fw, (unsigned)k, kThreads, 0, stream, args, false);
+    return e == cudaSuccess ? PER_OK : per_record_cuda(e);
+  }
   // one CTA, passes of `ncap` entries with every line prefetched, while the
   // passes stay few; larger batches take the grid path
-  const int T = t.num_levels - 1;
   int ncap = lines_ncap(t, n);
   if (!per_update_uses_grid(t, n)) {
     const void* fl = (const void*)per_update_lines_kernel;
