@@ -71,7 +71,7 @@ struct SampleArgs {
   int32_t group_bytes;     // staging bytes per group of four rows (gather4: 128-byte multiple)
   int32_t cp_bytes;        // cp.async piece size when not using bulk copies (4, 8, 16)
   int32_t pre_bytes;       // shared-memory bytes of the staged top level (128-byte multiple)
-  int32_t draws_per_warp;  // draws per warp and tile (32; fewer in wide mode)
+  int32_t draws_per_warp;  // draws per warp and tile (32 sharded; fewer for small batches and wide rows)
   int32_t wide;            // rows copied in this kernel piecewise by bulk copies (wide rows)
   int32_t wide_piece;      // wide mode: bytes per piece and per lane of the warp's tile
   int64_t num_tiles;
@@ -494,7 +494,9 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   const int nthreads = blockDim.x;
   const int nwarps = (nthreads >> 5) - 1;  // compute warps; the last warp is the helper
   const bool helper = warp == nwarps;
-  const int D = WIDE ? a.draws_per_warp : 32;  // draws per warp and tile (fewer for wide rows)
+  // draws per warp and tile: fewer than 32 for small batches (shorter row
+  // stores and gathers per warp) and wide rows; 32 when sharded
+  const int D = SHARDED ? 32 : a.draws_per_warp;
   const int64_t tile_draws = (int64_t)nwarps * D;
   const PerTree& t = a.t;
   PerScratch* sc = t.scratch;
@@ -1143,6 +1145,7 @@ struct Shape {
   int max_ctas;
   int sms;
   int slice;  // owned-only routing: global draws per CTA
+  int d;      // draws per warp
 };
 constexpr int kShapeSlots = 64;
 ShapeKey g_shape_key[kShapeSlots];
@@ -1322,7 +1325,6 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return per_record_cuda(e);
   if (a.world <= 1) a.owned_only = 0;  // one shard owns every draw: no routing pass
-  const int64_t warp_tiles = (a.batch + 31) / 32;
   // the shape chosen for this kernel, batch, world and store geometry is cached
   ShapeKey key{dev, fn, a.batch, a.owned_only ? a.world : 0, a.pre_bytes, a.stage_bytes};
   Shape sh;
@@ -1330,6 +1332,16 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     int sms = 148;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return per_record_cuda(e);
+    // draws per warp: a batch that leaves SMs without a full warp of draws
+    // is spread thinner (a multiple of 8, at least 8), which shortens every
+    // warp's row gather and row stores; 32 otherwise (and when sharded)
+    int d = 32;
+    if (!SHARDED) {
+      const int64_t per_sm = (a.batch + sms - 1) / sms;
+      d = (int)((per_sm + 7) / 8 * 8);
+      d = d < 8 ? 8 : d > 32 ? 32 : d;
+    }
+    const int64_t warp_tiles = (a.batch + d - 1) / d;
     int rc = per_set_smem(fn, (size_t)a.pre_bytes + (size_t)kMaxWarps * a.stage_bytes);
     if (rc) return rc;
     rc = per_set_smem(fn112, (size_t)a.pre_bytes + (size_t)(kR112Warps - 1) * a.stage_bytes);
@@ -1383,9 +1395,13 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
     sh.max_ctas = max_ctas;
     sh.sms = sms;
     sh.slice = best_slice;
+    sh.d = d;
     shape_store(key, sh);
   }
   const int64_t nw = sh.nw;
+  const int D = sh.d;
+  a.draws_per_warp = D;
+  const int64_t warp_tiles = (a.batch + D - 1) / D;
   // without four-row gathers: a few rows per SM take cp.async chains (lower
   // latency), many take bulk copies (more rows in flight)
   const int64_t busy_tiles = a.owned_only ? (warp_tiles + a.world - 1) / a.world : warp_tiles;
@@ -1398,7 +1414,7 @@ int launch_vec(SampleArgs a, cudaStream_t stream) {
   }
   const int threads = (int)(nw + 1) * 32;
   const size_t smem = (size_t)a.pre_bytes + (size_t)nw * a.stage_bytes;
-  a.num_tiles = (a.batch + nw * 32 - 1) / (nw * 32);
+  a.num_tiles = (a.batch + nw * D - 1) / (nw * D);
   int64_t grid;
   if (a.owned_only) {
     a.slice = sh.slice;
