@@ -192,7 +192,7 @@ int per_add(const per_store_t* store, const per_field_t* fields,
  * PER_ERR_TOO_LARGE. The first call on a device resolves the array's device
  * address (cudaGetSymbolAddress, with that device current): make it before
  * any stream capture; after cudaDeviceReset() on that device the cached
- * address is stale, so do not call it there again. Batches of up to 4096
+ * address is stale, so do not call it there again. Batches of up to 2048
  * indices use none of the array; larger ones first clear, on `stream`, the
  * words they use. Calls that overlap on the GPU share the array and race:
  * serialise them.

@@ -1,15 +1,11 @@
 """The update paths against the oracle (B200).
 
-Batches of up to 512 indices go through the partitioned update (CTAs owning
+Batches of up to 2048 indices go through the partitioned update (CTAs owning
 disjoint top-level nodes, each applying its entries in rounds of 32 with warp
-elections). Batches up to a few thousand indices go through the one-CTA
-prefetched update
-in passes of up to 512 entries; a later pass overwrites an earlier one, so
-the last occurrence of a slot still wins across passes. Larger batches take
-the grid path. Every path must give the oracle's leaves (last occurrence
-wins, within 1e-6) and exact tree sums, on trees of 3 and 4 levels. The
-sharded entry point with a device count applies only the counted prefix of
-its indices."""
+elections); larger batches take the grid path. Every path must give the
+oracle's leaves (last occurrence wins, within 1e-6) and exact tree sums, on
+trees of 2, 3 and 4 levels. The sharded entry point with a device count
+applies only the counted prefix of its indices."""
 
 import ctypes
 
@@ -35,7 +31,8 @@ def _dup_batch(rng, cap, n):
 
 @pytest.mark.parametrize("cap,n", [(1_000_000, 1), (1_000_000, 32), (1_000_000, 256),
                                    (1_000_000, 512), (100_000, 300), (20_000, 500),
-                                   (5_000_000, 400), (1_000_000, 300), (1_000_000, 513), (1_000_000, 1024),
+                                   (20_000, 2048), (5_000_000, 400), (5_000_000, 2049),
+                                   (1_000_000, 300), (1_000_000, 513), (1_000_000, 2048), (1_000_000, 1024),
                                    (1_000_000, 2500), (1_000_000, 4096), (1_000_000, 5000),
                                    (5_000_000, 700), (5_000_000, 3000)])
 def test_update_matches_oracle(cap, n):
@@ -59,7 +56,7 @@ def test_update_matches_oracle(cap, n):
 
 
 @pytest.mark.parametrize("n,count", [(400, 150), (512, 512), (256, 0), (600, 250),
-                                     (2048, 2048), (2048, 0), (4096, 1500)])
+                                     (2048, 2048), (2048, 0), (2048, 1999), (4096, 1500)])
 def test_shard_update_reads_only_the_counted_prefix(n, count):
     rng = np.random.default_rng(n + count)
     cap, base = 200_000, 400_000
@@ -109,16 +106,17 @@ def _apply_and_check(cap, leaves, batches):
 
 def test_partitioned_update_one_top_node_many_rounds():
     """512 entries under one top-level node (one CTA takes them all: 16
-    rounds of 32, duplicates across rounds): the last occurrence still wins."""
+    rounds of 32, duplicates across rounds): the last occurrence still wins;
+    then 2048 such entries (64 rounds)."""
     rng = np.random.default_rng(5)
     cap = 1_000_000
     leaves = cases.leaves_abs_normal(rng, cap)
     node = 321  # top-level node of a 1M store: slots 321 * 1024 ...
     batches = []
-    for _ in range(2):
-        idx = (node * 1024 + rng.integers(0, 1024, 512)).astype(np.int64)
-        idx[rng.integers(0, 512, 100)] = idx[rng.integers(0, 512, 100)]  # more duplicates
-        td = (rng.standard_normal(512) * 2).astype(np.float32)
+    for m in (512, 2048):
+        idx = (node * 1024 + rng.integers(0, 1024, m)).astype(np.int64)
+        idx[rng.integers(0, m, 100)] = idx[rng.integers(0, m, 100)]  # more duplicates
+        td = (rng.standard_normal(m) * 2).astype(np.float32)
         batches.append((idx, td))
     _apply_and_check(cap, leaves, batches)
 

@@ -53,7 +53,7 @@ def test_noalloc_update_matches_regular_entry_point():
     b = make_buffer(cap, {"x": 1}, None, leaves)
     sb = _store_without_scratch(b)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    for n in (6000, 20000, 300):  # two grid-path calls in a row, then the single-CTA path
+    for n in (6000, 20000, 300):  # two grid-path calls in a row, then the partitioned path
         idx, td = _batch(rng, cap, n)
         rc_a = _lib.lib.per_update_priorities(a._store_ref, idx.data_ptr(), td.data_ptr(), n, stream)
         rc_b = _lib.lib.per_update_priorities_noalloc(ctypes.byref(sb), idx.data_ptr(),

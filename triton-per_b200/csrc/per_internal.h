@@ -47,7 +47,7 @@ int per_launch_sample(const PerTree& t, const float* rand, const PerRng* rng, in
 int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int64_t n,
                       cudaStream_t stream);
 // True when per_launch_update() of n entries takes the grid path (claim words
-// and grid-barrier scratch); false for the single-CTA path, which uses neither.
+// and grid-barrier scratch); false for the partitioned path, which uses neither.
 bool per_update_uses_grid(const PerTree& t, int64_t n);
 // Update with global indices: slot = idx - base; indices outside the store
 // are errors when strict, else skipped and counted as another shard's.

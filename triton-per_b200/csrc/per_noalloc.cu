@@ -1,7 +1,7 @@
 // Priority update for callers that cannot allocate device memory.
 //
 // per_update_priorities() needs device scratch beyond its inputs and outputs
-// once a batch is too large for its single-CTA path (more than 1024
+// once a batch is too large for its partitioned path (more than 2048
 // indices): one claim word per slot and per tree node, which elect the one
 // writer of each slot and node, plus the words of a grid barrier. Its callers
 // allocate that scratch themselves and pass it in per_store_t (claims[],
@@ -23,7 +23,7 @@
 // it. Make that first call before any stream capture.
 //
 // All calls share the one array and it keeps the previous call's contents.
-// Batches of up to 4096 indices take the single-CTA path, which uses none of
+// Batches of up to 2048 indices take the partitioned path, which uses none of
 // it; a larger batch first clears, on its stream, the claim words and barrier
 // words that its grid uses (a grid that gave up at a bounded wait may have
 // left them set). Two calls whose work overlaps on the GPU (different streams,
@@ -103,7 +103,7 @@ extern "C" int per_update_priorities_noalloc(const per_store_t* s, const int64_t
   t.claims[2] = reinterpret_cast<uint32_t*>(base + kOffClaims2);
   t.scratch = reinterpret_cast<PerScratch*>(base + kOffBarrier);
 
-  // the single-CTA path touches none of the array; the grid path starts from
+  // the partitioned path touches none of the array; the grid path starts from
   // cleared barrier and claim words (the previous call's contents stay)
   cudaStream_t st = (cudaStream_t)stream;
   if (per_update_uses_grid(t, n)) {

@@ -13,9 +13,9 @@
 // Exactly one writer per slot and per node is elected, which makes the result
 // deterministic: for duplicate indices the last occurrence wins, and the sums
 // never drift.
-//   * small batches (<= 1024 indices): one CTA, election in shared-memory
-//     hash tables; per level the touched nodes are listed (warp counts, then
-//     offsets) and recomputed 32 per warp; levels separated by __syncthreads;
+//   * batches of up to 2048 indices: CTAs that each own the entries under a
+//     disjoint share of the top-level nodes (no coordination between CTAs),
+//     warp elections by match, every level summed by one warp;
 //   * larger batches: a co-resident grid, election with atomicMax on global
 //     claim words, levels separated by grid barriers; claims are reset by
 //     their owner in the phase that reads them, so the claim arrays are
@@ -149,284 +149,28 @@ __global__ void __launch_bounds__(kThreads) per_update_kernel(UpdateArgs a) {
   }
 }
 
-constexpr uint32_t kEmpty = 0xffffffffu;
-
-// ---------------------------------------------------------------- prefetched update
-// Batches of up to kLMaxN indices whose lines fit in shared memory. The nodes
-// that an update touches are known from the leaf indices alone (node of level
-// L = leaf >> 5L), so every 32-child line the recompute needs (children of
-// every touched node of every level) is fetched at once, right after the
-// election: one L2 round trip for the whole update instead of one per level.
-// The new values are then patched into the staged lines (winning leaves
-// first, then each recomputed node into its parent's line) and every level
-// is summed from shared memory. Node values are the same per_sum32_tree of
-// the same children as in the other update paths, so the tree bits do not
-// depend on the path.
-constexpr int kLPer = 2;                   // entries per thread
-constexpr int kLMaxN = kThreads * kLPer;   // 512
-constexpr int kLHashBits = 10;
-constexpr int kLHash = 1 << kLHashBits;    // load factor <= 1/2
-constexpr int kLMaxT = 4;                  // tree levels above the leaves
-constexpr size_t kLinesSmemMax = 200 * 1024;  // shared memory the kernel may ask for
-constexpr int kLinesMaxPasses = 8;            // beyond this many passes: the grid path
-
-__device__ __forceinline__ uint32_t lslot(uint32_t key) {
-  return (key * 2654435761u) >> (32 - kLHashBits);
-}
-
-__device__ __forceinline__ int lset_insert(uint32_t* keys, uint32_t key) {
-  uint32_t s = lslot(key);
-  for (int probe = 0; probe < kLHash; ++probe) {
-    const uint32_t prev = atomicCAS(&keys[s], kEmpty, key);
-    if (prev == kEmpty || prev == key) return (int)s;
-    s = (s + 1) & (kLHash - 1);
-  }
-  return -1;
-}
-
-// Shared-memory bytes of the prefetched update for T levels above the leaves
-// and up to ncap nodes per level.
-__host__ __device__ __forceinline__ size_t lines_smem(int T, int ncap) {
-  return (size_t)T * ncap * PER_LINE_STRIDE          // staged lines
-         + (size_t)(2 + 2 * T) * kLHash * 4          // election table, node sets + positions
-         + (size_t)2 * T * ncap * 4;                 // node lists + parents' set slots
-}
-
-__global__ void __launch_bounds__(kThreads, 1) per_update_lines_kernel(UpdateArgs a, int ncap) {
-  const PerTree& t = a.t;
-  const int T = t.num_levels - 1;
-  extern __shared__ __align__(16) unsigned char s_dyn[];
-  unsigned char* lines = s_dyn;            // [T][ncap] staged lines
-  uint32_t* wkey = reinterpret_cast<uint32_t*>(lines + (size_t)T * ncap * PER_LINE_STRIDE);
-  uint32_t* wval = wkey + kLHash;
-  uint32_t* skey = wval + kLHash;          // [T][kLHash] node sets
-  uint32_t* spos = skey + T * kLHash;      // [T][kLHash] list position of each set slot
-  uint32_t* list = spos + T * kLHash;      // [T][ncap] touched nodes per level
-  uint32_t* pslot = list + T * ncap;       // [T][ncap] set slot of the node's parent
-  __shared__ int s_cnt[kLMaxT];
-  __shared__ uint32_t s_max;
-  __shared__ uint32_t s_fresh[kThreads / 32][32];  // nodes a warp entered first, in list order
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const uint32_t lbase = per_smem_addr_generic(lines);
-
-  // the first pass's tables are cleared while the previous kernel may still run
-  for (int k = threadIdx.x; k < kLHash; k += kThreads) {
-    wkey[k] = kEmpty;
-    wval[k] = 0u;
-    for (int L = 0; L < T; ++L) skey[L * kLHash + k] = kEmpty;
-  }
-  if (threadIdx.x < kLMaxT) s_cnt[threadIdx.x] = 0;
-  if (threadIdx.x == 0) s_max = 0u;
-  per_wait_previous_grid();
-  // the first pass's entries are loaded together with the device count (a
-  // sharded update reads how many entries its sample owns): entries past the
-  // count are loaded (inside the caller's n) but not used
-  int64_t li[kLPer];
-  float tdv[kLPer];
-#pragma unroll
-  for (int q = 0; q < kLPer; ++q) {
-    const int64_t e = threadIdx.x + q * kThreads;
-    const bool in = e < a.n && e < ncap;
-    li[q] = in ? slot_of(a, e) : -1;
-    tdv[q] = in ? a.td[e] : 0.f;
-  }
-  const int64_t n = entries_of(a);
-
-  // passes of `ncap` entries in order; a later pass overwrites an earlier
-  // one's leaves, so the last occurrence of a slot wins across passes too
-  for (int64_t c0 = 0; c0 < n; c0 += ncap) {
-    if (c0 > 0) {
-      __syncthreads();
-      for (int k = threadIdx.x; k < kLHash; k += kThreads) {
-        wkey[k] = kEmpty;
-        wval[k] = 0u;
-        for (int L = 0; L < T; ++L) skey[L * kLHash + k] = kEmpty;
-      }
-      if (threadIdx.x < kLMaxT) s_cnt[threadIdx.x] = 0;
-      if (threadIdx.x == 0) s_max = 0u;
-    }
-    const int64_t c1 = min(c0 + ncap, n);
-#pragma unroll
-    for (int q = 0; q < kLPer; ++q) {
-      const int64_t e = c0 + threadIdx.x + q * kThreads;
-      if (c0 > 0) {
-        li[q] = e < c1 ? slot_of(a, e) : -1;
-        tdv[q] = e < c1 ? a.td[e] : 0.f;
-      } else if (e >= c1) {  // loaded past the device count: not an entry
-        li[q] = -1;
-        tdv[q] = 0.f;
-      }
-    }
-    __syncthreads();
-
-    // election (the last occurrence of a slot wins: largest position). Every
-    // valid entry also enters the node of each level above its leaf; the
-    // entry that adds a node first gives it a list position, and the warp
-    // fetches its new nodes' lines right away (the winner of a slot touches
-    // the same nodes)
-    int slot[kLPer], lslot0[kLPer];
-    float np[kLPer];
-    uint32_t tmax = 0u, nbad = 0u, nforeign = 0u;
-#pragma unroll
-    for (int q = 0; q < kLPer; ++q) {
-      const int64_t e = c0 + threadIdx.x + q * kThreads;
-      slot[q] = -1;
-      lslot0[q] = -1;
-      np[q] = 0.f;
-      // the same for every thread of the block: a pass past the last entry
-      // has nothing to elect (a batch of at most kThreads takes one)
-      if (c0 + (int64_t)q * kThreads >= c1) continue;
-      bool valid = false;
-      if (e < c1) {
-        if (li[q] < 0 || li[q] >= t.capacity) {
-          if (a.strict) ++nbad; else ++nforeign;
-        } else {
-          valid = true;
-          // the slot's table entry first: the atomics' round trips overlap powf
-          slot[q] = lset_insert(wkey, (uint32_t)li[q]);
-          np[q] = new_priority(t, tdv[q]);
-          tmax = max(tmax, __float_as_uint(np[q]));
-          if (slot[q] >= 0) atomicMax(&wval[slot[q]], (uint32_t)(e + 1));
-        }
-      }
-      uint32_t nd = valid ? (uint32_t)li[q] >> PER_LOG_FANOUT : 0u;
-      int below_p = -1;  // list position of the node entered at the level below, if new
-      for (int L = 0; L < T; ++L) {
-        int sl = -1;
-        bool fresh = false;
-        if (valid) {
-          uint32_t h = lslot(nd);
-          uint32_t* keys = skey + L * kLHash;
-          for (int probe = 0; probe < kLHash; ++probe) {
-            const uint32_t prev = atomicCAS(&keys[h], kEmpty, nd);
-            if (prev == kEmpty || prev == nd) {
-              sl = (int)h;
-              fresh = prev == kEmpty;
-              break;
-            }
-            h = (h + 1) & (kLHash - 1);
-          }
-        }
-        // list positions for the warp's new nodes: one shared counter add
-        const uint32_t m = __ballot_sync(PER_FULL_MASK, fresh);
-        int pbase = 0;
-        if (lane == 0 && m) pbase = atomicAdd(&s_cnt[L], __popc(m));
-        pbase = __shfl_sync(PER_FULL_MASK, pbase, 0);
-        const int newp = fresh ? pbase + __popc(m & ((1u << lane) - 1u)) : -1;
-        if (L == 0) lslot0[q] = sl;
-        if (below_p >= 0) pslot[(L - 1) * ncap + below_p] = (uint32_t)sl;  // parent of that node
-        const int nf = __popc(m);
-        if (fresh) {
-          list[L * ncap + newp] = nd;
-          spos[L * kLHash + sl] = (uint32_t)newp;
-          s_fresh[warp][newp - pbase] = nd;  // the node of the warp's (newp - pbase)-th new entry
-        }
-        __syncwarp();
-        // the warp fetches its new nodes' lines together, 4 lines (8 x 16 B
-        // each) per instruction: every node index is read first, then all
-        // the copies go out back to back
-        const float* clevel = t.levels[L];
-        const int part = lane & 7;
-        uint32_t gn[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int g = (lane >> 3) + 4 * i;
-          gn[i] = g < nf ? s_fresh[warp][g] : 0u;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int g = (lane >> 3) + 4 * i;
-          if (g < nf)
-            per_cp_async16(lbase + (uint32_t)((L * ncap + pbase + g) * PER_LINE_STRIDE + part * 16),
-                           clevel + (int64_t)gn[i] * PER_FANOUT + part * 4);
-        }
-        __syncwarp();
-        below_p = newp;
-        nd >>= PER_LOG_FANOUT;
-      }
-    }
-    if (nbad) {
-      per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
-      per_flag(t.status, PER_EVT_BAD_INDEX);
-    }
-    if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(PER_FULL_MASK, tmax, o));
-    if (lane == 0 && tmax) atomicMax(&s_max, tmax);
-    __syncthreads();
-    if (threadIdx.x == 0 && s_max) atomicMax(reinterpret_cast<unsigned int*>(t.max_priority), s_max);
-
-    // winners write their leaf; every thread waits for the lines it fetched
-    bool win[kLPer];
-#pragma unroll
-    for (int q = 0; q < kLPer; ++q) {
-      const int64_t e = c0 + threadIdx.x + q * kThreads;
-      win[q] = slot[q] >= 0 && wval[slot[q]] == (uint32_t)(e + 1);
-      if (win[q]) t.levels[0][li[q]] = np[q];
-    }
-    per_cp_async_wait_all();
-    __syncthreads();
-
-    // the winning leaves go into their chunk lines
-#pragma unroll
-    for (int q = 0; q < kLPer; ++q) {
-      if (win[q]) {
-        float* line = reinterpret_cast<float*>(lines + (size_t)spos[lslot0[q]] * PER_LINE_STRIDE);
-        line[li[q] & (PER_FANOUT - 1)] = np[q];
-      }
-    }
-    __syncthreads();
-
-    // level by level: sum each touched node's line, store it, patch it into
-    // its parent's line
-    for (int L = 0; L < T; ++L) {
-      for (int p = threadIdx.x; p < s_cnt[L]; p += kThreads) {
-        const uint32_t node = list[L * ncap + p];
-        const float4* row =
-            reinterpret_cast<const float4*>(lines + (size_t)(L * ncap + p) * PER_LINE_STRIDE);
-        float c[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 v = row[i];
-          c[4 * i] = v.x;
-          c[4 * i + 1] = v.y;
-          c[4 * i + 2] = v.z;
-          c[4 * i + 3] = v.w;
-        }
-        const float v = per_sum32_tree(c);
-        t.levels[L + 1][node] = v;
-        if (L + 1 < T) {
-          const uint32_t pp = spos[(L + 1) * kLHash + pslot[L * ncap + p]];
-          float* pline = reinterpret_cast<float*>(
-              lines + (size_t)((L + 1) * ncap + pp) * PER_LINE_STRIDE);
-          pline[node & (PER_FANOUT - 1)] = v;
-        }
-      }
-      __syncthreads();
-    }
-  }
-}
-
 // ---------------------------------------------------------------- partitioned update
-// Batches of up to kWMaxN indices: K one-warp CTAs, CTA k taking the entries
-// whose top-level ancestor (the node of level T above the leaf, T the highest
-// maintained level) hashes to k. Entries under different top-level nodes
-// touch disjoint nodes at every level, so the CTAs never coordinate: each
-// loads every entry, keeps its own in position order, and applies them in
-// rounds of 32 (one per lane). A round fetches every lane's line of every
-// level at once (duplicates included), elects the winner of each slot (the
-// highest lane among equal slots: the last occurrence) and the owner of each
-// touched node (the lowest lane among equal nodes) with warp matches while
-// the lines are in flight, then patches the winning leaves into their
-// owner's line and sums level by level, each owner patching its node into
-// the line of its parent's owner. Later rounds see earlier rounds' writes
-// (same warp, program order), so the last occurrence wins across rounds too.
-// Node values are per_sum32_tree of the same children as in the other update
-// paths.
-constexpr int kWMaxN = 512;              // entries of a batch
+// Batches of up to kWMaxN indices: K CTAs (a power of two), CTA k taking the
+// entries whose top-level ancestor (the node of level T above the leaf, T the
+// highest maintained level) hashes to k. Entries under different top-level
+// nodes touch disjoint nodes at every level, so the CTAs never coordinate:
+// each loads every entry, keeps its own in position order, and its warp 0
+// applies them in rounds of 32 (one per lane) while the other warps compute
+// the new priorities. A round fetches every lane's line of every level at
+// once (duplicates included), elects the winner of each slot (the highest
+// lane among equal slots: the last occurrence) and the owner of each touched
+// node (the lowest lane among equal nodes) with warp matches while the lines
+// are in flight, then patches the winning leaves into their owner's line and
+// sums level by level, each owner patching its node into the line of its
+// parent's owner. Later rounds see earlier rounds' writes (same warp, program
+// order), so the last occurrence wins across rounds too. Node values are
+// per_sum32_tree of the same children as in the grid path.
+constexpr int kWMaxN = 2048;             // entries of a batch
 constexpr int kWEntriesPerCta = 16;      // expected entries per CTA
-constexpr int kWMaxT = 4;                // tree levels above the leaves
+constexpr int kWMaxT = 4;                // tree levels above the leaves (capacity <= 2^30)
+constexpr int kWPer = kWMaxN / kThreads; // entries per thread
+constexpr int kWarps = kThreads / 32;
+static_assert(kWPer * kWarps <= 64, "warp counts scanned by one warp, two per lane");
 
 // Named barrier 1 between the priority warps (arrive) and warp 0 (sync).
 __device__ __forceinline__ void named_bar_arrive_upd(int count) {
@@ -461,9 +205,7 @@ __device__ __forceinline__ void warp_issue_lines(const float* level, unsigned ch
   }
 }
 
-constexpr int kWPer = kWMaxN / kThreads;  // entries per thread
-
-__global__ void __launch_bounds__(kThreads) per_update_warp_kernel(UpdateArgs a) {
+__global__ void __launch_bounds__(kThreads) per_update_part_kernel(UpdateArgs a) {
   const PerTree& t = a.t;
   const int T = t.num_levels - 1;
   const int lane = threadIdx.x & 31;
@@ -471,16 +213,24 @@ __global__ void __launch_bounds__(kThreads) per_update_warp_kernel(UpdateArgs a)
   __shared__ uint32_t s_leaf[kWMaxN];  // this CTA's entries in position order (slots < 2^30)
   __shared__ float s_td[kWMaxN];
   __shared__ float s_np[kWMaxN];       // their new priorities
-  __shared__ int s_wcnt[kWPer][kThreads / 32];
+  __shared__ int s_wcnt[kWPer * kWarps];  // entries of (step q, warp w) at q * kWarps + w
+  __shared__ int s_woff[kWPer * kWarps + 1];  // their offsets in position order, then the total
   __shared__ __align__(16) unsigned char s_lines[kWMaxT][32 * PER_LINE_STRIDE];
   per_wait_previous_grid();
+  // entries threadIdx.x + q * kThreads for the steps q the batch reaches
+  const int steps = (int)((a.n + kThreads - 1) / kThreads);
   int64_t li[kWPer];
   float tv[kWPer];
 #pragma unroll
   for (int q = 0; q < kWPer; ++q) {
+    li[q] = -1;
+    tv[q] = 0.f;
+    if (q >= steps) continue;  // the same for the whole block
     const int64_t e = threadIdx.x + q * kThreads;
-    li[q] = e < a.n ? slot_of(a, e) : -1;
-    tv[q] = e < a.n ? a.td[e] : 0.f;
+    if (e < a.n) {
+      li[q] = slot_of(a, e);
+      tv[q] = a.td[e];
+    }
   }
   const int64_t n = entries_of(a);
   // this CTA's entries (those whose top-level ancestor hashes to it), in
@@ -492,6 +242,9 @@ __global__ void __launch_bounds__(kThreads) per_update_warp_kernel(UpdateArgs a)
   uint32_t mm[kWPer];
 #pragma unroll
   for (int q = 0; q < kWPer; ++q) {
+    mine[q] = false;
+    mm[q] = 0u;
+    if (q >= steps) continue;
     const int64_t e = threadIdx.x + q * kThreads;
     const bool in = e < n;
     const bool valid = in && li[q] >= 0 && li[q] < t.capacity;
@@ -500,7 +253,7 @@ __global__ void __launch_bounds__(kThreads) per_update_warp_kernel(UpdateArgs a)
     }
     mine[q] = valid && top_cta((uint32_t)li[q] >> tshift, kmask) == blockIdx.x;
     mm[q] = __ballot_sync(PER_FULL_MASK, mine[q]);
-    if (lane == 0) s_wcnt[q][warp] = __popc(mm[q]);
+    if (lane == 0) s_wcnt[q * kWarps + warp] = __popc(mm[q]);
   }
   if (nbad) {
     per_count(t.status, PER_STATUS_BAD_INDICES, nbad);
@@ -508,17 +261,34 @@ __global__ void __launch_bounds__(kThreads) per_update_warp_kernel(UpdateArgs a)
   }
   if (nforeign) per_count(t.status, PER_STATUS_FOREIGN, nforeign);
   __syncthreads();
-  int cnt = 0;
+  if (warp == 0) {  // offsets of the (step, warp) groups: one warp scan, two per lane
+    const int nseg = steps * kWarps;
+    const int c0 = lane < nseg ? s_wcnt[lane] : 0;
+    const int c1 = lane + 32 < nseg ? s_wcnt[lane + 32] : 0;
+    int x0 = c0, x1 = c1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y0 = __shfl_up_sync(PER_FULL_MASK, x0, o);
+      const int y1 = __shfl_up_sync(PER_FULL_MASK, x1, o);
+      if (lane >= o) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    const int tot0 = __shfl_sync(PER_FULL_MASK, x0, 31);
+    s_woff[lane] = x0 - c0;
+    s_woff[lane + 32] = tot0 + x1 - c1;
+    if (lane == 31) s_woff[kWPer * kWarps] = tot0 + x1;
+  }
+  __syncthreads();
+  const int cnt = s_woff[kWPer * kWarps];
 #pragma unroll
   for (int q = 0; q < kWPer; ++q) {
-#pragma unroll
-    for (int w = 0; w < kThreads / 32; ++w) {
-      if (w == warp && mine[q]) {
-        const int r = cnt + __popc(mm[q] & ((1u << lane) - 1u));
-        s_leaf[r] = (uint32_t)li[q];
-        s_td[r] = tv[q];
-      }
-      cnt += s_wcnt[q][w];
+    if (q >= steps) continue;
+    if (mine[q]) {
+      const int r = s_woff[q * kWarps + warp] + __popc(mm[q] & ((1u << lane) - 1u));
+      s_leaf[r] = (uint32_t)li[q];
+      s_td[r] = tv[q];
     }
   }
   __syncthreads();
@@ -708,24 +478,8 @@ int per_launch_update(const PerTree& t, const int64_t* idx, const float* td, int
   return per_launch_update_shard(t, 0, 1, idx, td, n, nullptr, stream);
 }
 
-namespace {
-
-// Entries per pass of the single-CTA prefetched update for this tree and
-// batch (0 when it cannot serve the tree).
-int lines_ncap(const PerTree& t, int64_t n) {
-  const int T = t.num_levels - 1;
-  if (T > kLMaxT) return 0;
-  const int64_t want = n < kLMaxN ? n : kLMaxN;
-  for (int c = (int)((want + 31) / 32 * 32); c >= 32; c -= 32)
-    if (lines_smem(T, c) <= kLinesSmemMax) return c;
-  return 0;
-}
-
-}  // namespace
-
 bool per_update_uses_grid(const PerTree& t, int64_t n) {
-  const int ncap = lines_ncap(t, n);
-  return !(ncap > 0 && n <= (int64_t)kLinesMaxPasses * ncap);
+  return !(n <= kWMaxN && t.num_levels - 1 <= kWMaxT);
 }
 
 int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, const int64_t* idx,
@@ -739,10 +493,9 @@ int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, cons
   a.strict = strict;
   a.count = reinterpret_cast<const unsigned long long*>(count);
   const int T = t.num_levels - 1;
-  // up to kWMaxN entries: one-warp CTAs, each owning the entries under its
-  // share of the top-level nodes
-  if (n <= kWMaxN && T <= kWMaxT) {
-    const void* fw = (const void*)per_update_warp_kernel;
+  // up to kWMaxN entries: CTAs owning disjoint shares of the top-level nodes
+  if (!per_update_uses_grid(t, n)) {
+    const void* fw = (const void*)per_update_part_kernel;
     // a power of two near n / kWEntriesPerCta, at most the top level's nodes
     int64_t k = 1;
     while (k * kWEntriesPerCta < n && 2 * k <= t.level_len[T]) k *= 2;
@@ -750,18 +503,7 @@ int per_launch_update_shard(const PerTree& t, int64_t base, int32_t strict, cons
     cudaError_t e = per_launch(fw, (unsigned)k, kThreads, 0, stream, args, false);
     return e == cudaSuccess ? PER_OK : per_record_cuda(e);
   }
-  // one CTA, passes of `ncap` entries with every line prefetched, while the
-  // passes stay few; larger batches take the grid path
-  int ncap = lines_ncap(t, n);
-  if (!per_update_uses_grid(t, n)) {
-    const void* fl = (const void*)per_update_lines_kernel;
-    const size_t smem = lines_smem(T, ncap);
-    int rc = per_set_smem(fl, kLinesSmemMax);
-    if (rc) return rc;
-    void* args[] = {&a, &ncap};
-    cudaError_t e = per_launch(fl, 1, kThreads, smem, stream, args, false);
-    return e == cudaSuccess ? PER_OK : per_record_cuda(e);
-  }
+  // larger batches: the co-resident grid
   const void* fn = (const void*)per_update_kernel;
   int grid = 0;
   int rc = grid_for(fn, n, &grid);
