@@ -351,7 +351,8 @@ __device__ __forceinline__ PerMailbox* mailbox_of(PerMailbox* const* mailboxes, 
 constexpr int kBarMaxReady = 1;   // compute warps arrive: the CTA max is in s_cta_max
 constexpr int kBarGmaxReady = 2;  // helper arrives: the global max is in s_gmax
 constexpr int kMaxGrid = PER_MAX_GRID / 4;  // CTAs of one launch: one two-word slot each
-constexpr int kBarRouted = 3;  // compute warps: the CTA's owned draws are queued
+constexpr int kBarRouted = 3;  // all warps: the CTA's owned draws are queued
+constexpr int kBarBase = 4;    // helper arrives: the CTA's first output slot is in s_cbase
 constexpr int kSliceMax = 1024;  // owned-only routing: global draws per CTA
 constexpr int kAllToAllCtas = 64;  // max exchange: every CTA reads every slot up to this grid
 
@@ -477,6 +478,7 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   __shared__ uint64_t s_mbar[kMaxWarps];
   __shared__ uint32_t s_cta_max;
   __shared__ uint32_t s_cta_own;  // sharded: draws this CTA owns (compacted)
+  __shared__ unsigned long long s_cbase;  // owned-only routing: the CTA's first output slot
   __shared__ float s_gmax;
   __shared__ double s_stats[SHARDED ? PER_MAX_SHARDS : 1][2];
   __shared__ unsigned long long s_seq;
@@ -485,6 +487,7 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   // owned-only routing: this CTA's owned draws (offsets in its slice), and the
   // output ranges its warps wrote (for the in-kernel normalisation)
   __shared__ int32_t s_q[SHARDED ? kSliceMax : 1];
+  __shared__ float s_qu[SHARDED ? kSliceMax : 1];  // their uniforms (drawn once, while routing)
   __shared__ int32_t s_qn;
   __shared__ unsigned long long s_tbase[SHARDED ? kSliceMax / 32 : 1];
   __shared__ int32_t s_tcnt[SHARDED ? kSliceMax / 32 : 1];
@@ -575,9 +578,13 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
       loc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
     }
     // this lane's first uniform, while the scan below waits on shuffles
+    // (owned-only routing: the first draw this lane routes)
     if (!helper && !(SHARDED && a.owned_only) && lane < D) {
       const int64_t j = tile * tile_draws + warp * D + lane;
       if (tile < a.num_tiles && j < a.batch) rnd0 = draw_uniform(a, cbase, j);
+    } else if (!helper && SHARDED && a.owned_only) {
+      const int64_t j = (int64_t)blockIdx.x * a.slice + warp * 32 + lane;
+      if (j < min((int64_t)blockIdx.x * a.slice + a.slice, a.batch)) rnd0 = draw_uniform(a, cbase, j);
     }
     const double incl = per_warp_scan_incl(loc, lane);
     if (lane == 31) s_wsum[warp] = incl;
@@ -666,6 +673,19 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
   }
 
   if (helper) {
+    if (SHARDED && a.owned_only) {
+      // owned-only routing: once the CTA's owned draws are queued, reserve
+      // their output slots with one atomic (the compute warps read the base
+      // after their searches, by which time it has long returned)
+      named_bar_sync(kBarRouted, nthreads);
+      if (lane == 0) {
+        const uint32_t q = (uint32_t)s_qn;
+        s_cbase = q ? atomicAdd(&sc->draws[gen & 1u], (unsigned long long)q) : 0ull;
+        s_cta_own = q;
+      }
+      __syncwarp();
+      named_bar_arrive(kBarBase, nthreads);
+    }
     // ---- helper warp: exchange the batch max with the other CTAs while the
     // compute warps gather their rows
     if (SHARDED && a.p2p && blockIdx.x == 0) {  // peers' mailboxes, for the max put
@@ -844,8 +864,10 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     for (int64_t j0 = s0; j0 < s1; j0 += (int64_t)nwarps * 32) {
       const int64_t j = j0 + tc;
       bool mine = false;
+      float uj = 0.f;
       if (j < s1) {
-        const double r = (double)__fmul_rn(draw_uniform(a, cbase, j), total);
+        uj = j0 == s0 ? rnd0 : draw_uniform(a, cbase, j);
+        const double r = (double)__fmul_rn(uj, total);
         double S = 0.0;
         int owner = -1, lastpos = 0;
         for (int g = 0; g < a.world; ++g) {
@@ -861,14 +883,19 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
       int qb = 0;
       if (lane == 0 && m) qb = atomicAdd(&s_qn, __popc(m));
       qb = __shfl_sync(PER_FULL_MASK, qb, 0);
-      if (mine) s_q[qb + __popc(m & ((1u << lane) - 1u))] = (int32_t)(j - s0);
+      if (mine) {
+        const int qp = qb + __popc(m & ((1u << lane) - 1u));
+        s_q[qp] = (int32_t)(j - s0);
+        s_qu[qp] = uj;
+      }
     }
-    named_bar_sync(kBarRouted, nwarps * 32);
+    named_bar_sync(kBarRouted, nthreads);  // with the helper, which reserves the slots
     ntiles = (s_qn + 31) / 32;
     tstep = nwarps;
     tile = warp;
     if (tile >= ntiles) {  // no draws for this warp: nothing to add to the CTA max
       __syncwarp();
+      named_bar_sync(kBarBase, nthreads);  // every compute warp passes it once
       named_bar_arrive(kBarMaxReady, nthreads);
     }
   }
@@ -881,27 +908,24 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     const int64_t wj0 = tile * tile_draws + warp * D;  // first draw of this warp
     int64_t j = wj0 + lane;
     bool ok = lane < D && j < a.batch;
-    if (owned_mode) {
+    float rnd;
+    if (owned_mode) {  // a queued draw: its position and the uniform routing drew
       const int64_t k = tile * 32 + lane;
       ok = k < s_qn;
       j = ok ? s0 + s_q[k] : 0;
+      rnd = ok ? s_qu[k] : 0.f;
+    } else {
+      rnd = tile == blockIdx.x ? rnd0 : (ok ? draw_uniform(a, cbase, j) : 0.f);
     }
-    const float rnd = owned_mode ? (ok ? draw_uniform(a, cbase, j) : 0.f)
-                      : tile == blockIdx.x ? rnd0
-                                           : (ok ? draw_uniform(a, cbase, j) : 0.f);
 
     const float u = __fmul_rn(rnd, total);
     double r = (double)u;
     bool own = ok;
     unsigned long long obase = 0ull;  // sharded: first output slot of this warp's draws
     uint32_t om = 0u;
-    if (owned_mode) {
+    if (owned_mode) {  // the tile's slots follow the CTA's base (reserved by the helper)
       r -= base64;
       om = __ballot_sync(PER_FULL_MASK, own);
-      if (lane == 0 && om) {
-        obase = atomicAdd(&sc->draws[gen & 1u], (unsigned long long)__popc(om));
-        atomicAdd(&s_cta_own, (uint32_t)__popc(om));
-      }
     } else if (SHARDED) {
       // the shard whose range of the global prefix holds u (the last shard
       // with mass if u is at or past the total)
@@ -997,7 +1021,12 @@ __device__ __forceinline__ void sample_body(const SampleArgs& a, const CUtensorM
     int nrows;
     int orank = 0;
     if (SHARDED) {  // compact the owned draws into [obase, obase + popc(om))
-      obase = __shfl_sync(PER_FULL_MASK, obase, 0);
+      if (owned_mode) {
+        if (first_tile) named_bar_sync(kBarBase, nthreads);  // once per compute warp
+        obase = s_cbase + (unsigned long long)tile * 32ull;
+      } else {
+        obase = __shfl_sync(PER_FULL_MASK, obase, 0);
+      }
       if (owned_mode && lane == 0) {
         s_tbase[tile] = obase;
         s_tcnt[tile] = __popc(om);
