@@ -364,21 +364,6 @@ __device__ __forceinline__ uint32_t per_smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
 
-// Atomics on shared memory named by a generic pointer into it, issued as
-// shared-space atomics (a generic atomic takes the slower global path).
-__device__ __forceinline__ uint32_t per_atoms_cas(uint32_t* p, uint32_t cmp, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.shared.cas.b32 %0, [%1], %2, %3;"
-               : "=r"(old)
-               : "r"(per_smem_addr(p)), "r"(cmp), "r"(v)
-               : "memory");
-  return old;
-}
-
-__device__ __forceinline__ void per_atoms_max(uint32_t* p, uint32_t v) {
-  asm volatile("red.shared.max.u32 [%0], %1;" ::"r"(per_smem_addr(p)), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ void per_mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(per_smem_addr(bar)), "r"(count)
                : "memory");
