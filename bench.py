@@ -354,14 +354,16 @@ def time_replays(g, iters, world):
     return a.elapsed_time(b)  # ms
 
 
-def kernel_time_us(buf, batch, reps=20, launches=16, seed=7, beta=BETA):
-    """Average CUDA-event time of one fused-sample launch (graph of `launches`)."""
-    g0 = torch.Generator(device=buf.device).manual_seed(seed)
-    rands = [torch.rand(batch, generator=g0, device=buf.device) for _ in range(launches)]
+def kernel_time_us(buf, batch, reps=20, launches=16, beta=BETA):
+    """Average CUDA-event time of one fused-sample launch (graph of `launches`).
+    Uniforms are drawn inside the kernel from the buffer's advancing stream,
+    so every launch of every replay gathers new rows: a replayed set of fixed
+    uniforms would gather the same rows each time, which then come from L2
+    instead of HBM for batches whose rows fit in it."""
 
     def fn():
-        for r in rands:
-            buf.sample_from_uniforms(r, beta)
+        for _ in range(launches):
+            buf.sample(batch, beta)
 
     g = capture(fn, warm=2)
     for _ in range(3):
@@ -1069,7 +1071,9 @@ def main():
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic_from_profiles("sample_1Mx74_b256"),
                 "peak_source": peak_kind, "kernel": "per_sample_kernel_r112 (fused sample, 112-register build)",
-                "kernel_us": k_us, "algo_bytes_per_launch": ab, "batch": BATCH}
+                "kernel_us": k_us, "algo_bytes_per_launch": ab, "batch": BATCH,
+                "timing": "CUDA events over graph replays of back-to-back launches, uniforms drawn "
+                          "in the kernel (new rows every launch)"}
     # the same kernel at the large-batch end of the sweep (1M x 74, batch 65,536)
     k64 = kernel_time_us(buf, 65536, reps=10, launches=8)
     ab64 = algo_bytes(65536, ROW_DIM)
